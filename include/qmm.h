@@ -1,0 +1,228 @@
+/*
+ * qmm.h - C ABI of the B200 quantized-matmul library (libqmm_b200.so).
+ *
+ * The library replaces one hot path of mlx-runner: the quantized linear
+ * layer that every projection of its model runs through,
+ *     y = x . dequant(W)^T
+ * for MLX's mxfp8 (E4M3 codes, group 32, UE8M0 scales) and nvfp4 (E2M1
+ * codes, group 16, UE4M3 scales) formats on MLX's packed layout: codes
+ * U32 [N, K*bits/32] (LSB-first), scales U8 [N, K/group].
+ *
+ * Conventions shared by every entry point:
+ *   - return 0 (QMM_OK) on success or a qmm_status code; the message of the
+ *     first failure is latched and can be read with qmm_last_error();
+ *   - pointers named *_dev are device pointers of the current CUDA device;
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy stream);
+ *   - work is enqueued on `stream` and runs asynchronously; nothing here
+ *     synchronizes the device except qmm_weight_create/destroy;
+ *   - no entry point ever calls exit() and none falls back to the CPU;
+ *   - x and y are bf16 (uint16 bit patterns), row-major with a row stride.
+ *
+ * Reference interfaces replaced (paths relative to the mlx-runner tree):
+ *   src/mlx.zig:265      mlx_quantized_matmul    -> qmm_quantized_matmul, qmm_run
+ *   src/mlx.zig:274      mlx_dequantize          -> qmm_dequantize
+ *   src/mlx.zig:41-51    mlx_optional_int        -> qmm_optional_int
+ *   src/mlx.zig:589-595  check (int status)      -> qmm_status return codes
+ *   src/mlx.zig:719-805  error latch             -> qmm_last_error, qmm_error_pending
+ *   src/mlx.zig:562-595  fault.arm (test hook)   -> qmm_fault_arm
+ *   src/weights.zig:23-55  WeightsError, DType, QuantMode, QuantSpec
+ *   src/weights.zig:132-185 inferQuantSpec       -> qmm_infer_quant_spec
+ *   src/weights.zig:203-353 WeightMap (U32/U8 upload) -> qmm_weight_create
+ *   src/model.zig:218-258 namedLinearQ / qlinear -> qmm_linear, qmm_run
+ */
+#ifndef QMM_B200_H
+#define QMM_B200_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMM_ABI_VERSION 1
+
+/* Status codes.  1-9 mirror src/weights.zig:23-33 WeightsError and
+ * src/model.zig ModelError.MissingWeight; 20+ are device-side failures. */
+typedef enum qmm_status {
+    QMM_OK = 0,
+    QMM_ERR_BAD_SHAPE = 1,            /* shapes disagree (x K vs W K, group divisibility, ...) */
+    QMM_ERR_NONSTANDARD_QUANT = 2,    /* WeightsError.NonstandardQuant  (weights.zig:30) */
+    QMM_ERR_INCONSISTENT_QUANT = 3,   /* WeightsError.InconsistentQuant (weights.zig:31) */
+    QMM_ERR_AFFINE_UNSUPPORTED = 4,   /* WeightsError.AffineUnsupported (weights.zig:32) */
+    QMM_ERR_UNSUPPORTED_DTYPE = 5,    /* WeightsError.UnsupportedDtype  (weights.zig:26) */
+    QMM_ERR_BAD_MODE = 6,             /* mode string not "mxfp8"/"nvfp4", or group/bits mismatch */
+    QMM_ERR_BAD_ARGUMENT = 7,         /* NULL pointer, transpose=false, biases given, bad stride */
+    QMM_ERR_MISSING_WEIGHT = 8,       /* ModelError.MissingWeight (model.zig:220, :228) */
+    QMM_ERR_CUDA = 20,                /* a CUDA runtime/driver call failed */
+    QMM_ERR_OUT_OF_MEMORY = 21,       /* device allocation failed */
+    QMM_ERR_NCCL = 22,                /* an NCCL call failed or NCCL could not be loaded */
+    QMM_ERR_TIMEOUT = 23,             /* a bounded device-side wait gave up */
+    QMM_ERR_NO_DEVICE = 24,           /* the current device is not an sm_100 part */
+    QMM_ERR_INJECTED = 30             /* failure injected by qmm_fault_arm */
+} qmm_status;
+
+/* src/weights.zig:42 QuantMode. */
+typedef enum qmm_mode { QMM_MODE_NONE = 0, QMM_MODE_MXFP8 = 1, QMM_MODE_NVFP4 = 2 } qmm_mode;
+
+/* src/weights.zig:35 DType (the safetensors dtypes the loader accepts). */
+typedef enum qmm_dtype {
+    QMM_DTYPE_BF16 = 0, QMM_DTYPE_F32 = 1, QMM_DTYPE_U32 = 2, QMM_DTYPE_U8 = 3
+} qmm_dtype;
+
+/* src/weights.zig:43-55 QuantSpec. */
+typedef struct qmm_quant_spec {
+    int32_t mode;        /* qmm_mode */
+    int32_t group_size;  /* 32 (mxfp8), 16 (nvfp4), 0 (none) */
+    int32_t bits;        /* 8 (mxfp8), 4 (nvfp4), 0 (none) */
+} qmm_quant_spec;
+
+/* src/weights.zig:56-60 TensorInfo (one safetensors header entry). */
+typedef struct qmm_tensor_info {
+    const char* name;      /* NUL-terminated tensor name */
+    int32_t dtype;         /* qmm_dtype */
+    int32_t ndim;
+    const int64_t* shape;  /* ndim extents */
+} qmm_tensor_info;
+
+/* src/mlx.zig:41-51 mlx_optional_int: same layout (int, then bool). */
+typedef struct qmm_optional_int {
+    int value;
+    bool has_value;
+} qmm_optional_int;
+
+typedef struct qmm_weight qmm_weight;  /* opaque, owns device copies of codes + scales */
+typedef struct qmm_comm qmm_comm;      /* opaque tensor-parallel communicator (NCCL) */
+
+/* ---- spec inference (pure host; src/weights.zig:132-185) --------------- */
+
+/* Infer (mode, group, bits) from the tensor infos of a whole checkpoint,
+ * exactly as inferQuantSpec does: the first "*.scales" decides the ratio
+ * r = packed_cols / scale_cols (8 -> mxfp8, 2 -> nvfp4), every scales
+ * tensor must agree and every U32 "*.weight" needs its scales.  No scales
+ * and no U32/U8 tensor -> mode NONE. */
+int qmm_infer_quant_spec(const qmm_tensor_info* infos, int64_t count, qmm_quant_spec* out);
+
+/* Mode string for a spec: "mxfp8" / "nvfp4" (src/weights.zig:47-53; NONE
+ * maps to "mxfp8" there too, and is never used for a qmm). */
+const char* qmm_mode_str(qmm_quant_spec spec);
+
+/* Resolve mlx_quantized_matmul's (group_size, bits, mode) arguments into a
+ * spec; unset optionals take the mode's defaults (32/8, 16/4). */
+int qmm_spec_from_args(qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
+                       qmm_quant_spec* out);
+
+/* ---- stateless operator (src/mlx.zig:265 mlx_quantized_matmul) ----------- */
+
+/* y[M, N] = x[M, K] . dequant(w, scales)^T on `stream`.
+ *   x_dev      bf16 [M, K], row stride ldx (elements)
+ *   w_dev      U32  [w_rows = N, w_cols = K*bits/32]
+ *   scales_dev U8   [s_rows = N, s_cols = K/group]
+ *   biases     must be NULL (mxfp8/nvfp4 are bias-less, src/model.zig:230-232)
+ *   transpose  must be true (the only form the reference uses, model.zig:253)
+ *   y_dev      bf16 [M, N], row stride ldy (elements)
+ * Reads the scales in their checkpoint layout; needs no workspace. */
+int qmm_quantized_matmul(void* y_dev, int64_t ldy,
+                         const void* x_dev, int64_t m, int64_t k, int64_t ldx,
+                         const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
+                         const uint8_t* scales_dev, int64_t s_rows, int64_t s_cols,
+                         const void* biases, bool transpose,
+                         qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
+                         void* stream);
+
+/* ---- resident weights (src/weights.zig:203-353 + src/model.zig:244) ----- */
+
+#define QMM_SRC_HOST   0  /* codes/scales pointers are host memory */
+#define QMM_SRC_DEVICE 1  /* codes/scales pointers are device memory (copied) */
+
+/* Upload one quantized weight to the current device: the packed codes are
+ * copied bit for bit, the scales once into the kernels' tiled layout, and
+ * the split-K workspace is sized here so qmm_run never allocates.
+ *   n, k   logical W shape (out features, in features)
+ *   ldw    bytes between source code rows   (0: K*bits/8)
+ *   lds    bytes between source scale rows  (0: K/group)
+ * Blocks until the copies are done. */
+int qmm_weight_create(const void* codes, const void* scales, int64_t n, int64_t k,
+                      int64_t ldw, int64_t lds, qmm_quant_spec spec, int src_kind,
+                      void* stream, qmm_weight** out);
+
+/* Tensor-parallel shard of a full [n_full, k_full] weight: axis 0 takes the
+ * rows [rank*n_full/P, (rank+1)*n_full/P) (column-parallel), axis 1 the
+ * columns [rank*k_full/P, ...) (row-parallel).  A K-shard must start on a
+ * group boundary and a whole U32 word. */
+int qmm_weight_create_shard(const void* codes, const void* scales, int64_t n_full,
+                            int64_t k_full, qmm_quant_spec spec, int src_kind, int axis,
+                            int rank, int nranks, void* stream, qmm_weight** out);
+
+/* The slice qmm_weight_create_shard takes (pure host): rows [*row0, *row0 +
+ * *rows) and logical columns [*col0, *col0 + *cols) of the full weight. */
+int qmm_shard_range(int64_t n_full, int64_t k_full, qmm_quant_spec spec, int axis, int rank,
+                    int nranks, int64_t* row0, int64_t* rows, int64_t* col0, int64_t* cols);
+
+int qmm_weight_destroy(qmm_weight* w);
+
+/* n, k, spec and the device the weight lives on. */
+int qmm_weight_info(const qmm_weight* w, int64_t* n, int64_t* k, qmm_quant_spec* spec,
+                    int* device);
+
+/* y[M, N] = x[M, K] . dequant(W)^T.  transpose must be true.  Calls on the
+ * same handle must be ordered (same stream or externally synchronized):
+ * the split-K workspace belongs to the handle. */
+int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* y_dev,
+            int64_t ldy, bool transpose, void* stream);
+
+/* src/model.zig:218-233 namedLinearQ for one projection: `w` NULL with
+ * `has_packed_u32` set is MissingWeight (a packed tensor without scales);
+ * otherwise it forwards to qmm_run. */
+int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m,
+               int64_t ldx, void* y_dev, int64_t ldy, void* stream);
+
+/* src/mlx.zig:274 mlx_dequantize: out[N, K] in bf16 (out_dtype BF16) or fp32
+ * (F32).  Every mxfp8/nvfp4 value is exact in fp32; bf16 is exact unless a
+ * value leaves bf16's range. */
+int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dtype, void* stream);
+
+/* ---- tensor parallel (NCCL over NVLink) ----------------------------------- */
+
+/* 128-byte NCCL unique id, produced on one rank and broadcast by the caller. */
+int qmm_tp_unique_id(void* id128);
+/* One communicator per rank (current device).  max_partial_elems sizes the
+ * fp32 partial-sum buffer of qmm_tp_run_rowparallel (m * n at most), which
+ * is allocated here so the run itself never allocates. */
+int qmm_tp_comm_create(const void* id128, int nranks, int rank, int64_t max_partial_elems,
+                       qmm_comm** out);
+int qmm_tp_comm_destroy(qmm_comm* c);
+
+/* In-place bf16 sum all-reduce of `count` elements on `stream`. */
+int qmm_tp_allreduce_bf16(qmm_comm* c, void* buf_dev, int64_t count, void* stream);
+
+/* Row-parallel projection: y = allreduce_sum(x_shard . W_shard^T), with x_dev
+ * this rank's K-slice.  The partials are summed in fp32 and rounded to bf16
+ * once.  Column-parallel shards need no collective: use qmm_run on them. */
+int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const void* x_dev, int64_t m,
+                           int64_t ldx, void* y_dev, int64_t ldy, void* stream);
+
+/* ---- errors and test hooks ------------------------------------------------ */
+
+/* Copy the latched message of the first failure since the last call into
+ * buf (NUL-terminated, truncated to len) and clear the latch.  Returns the
+ * latched status (QMM_OK if none).  src/mlx.zig:792 takeError. */
+int qmm_last_error(char* buf, size_t len);
+
+/* 1 when a failure is latched (src/mlx.zig:778 errorPending). */
+int qmm_error_pending(void);
+
+/* Make the k-th checked entry-point call from now fail with QMM_ERR_INJECTED
+ * (k >= 1; 0 disarms).  Mirrors the test-only src/mlx.zig:562-595 fault.arm;
+ * the failure is injected on the host before any device work is enqueued. */
+int qmm_fault_arm(uint64_t k);
+/* 1 if the armed fault fired (src/mlx.zig:581 didFire). */
+int qmm_fault_fired(void);
+
+int qmm_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QMM_B200_H */

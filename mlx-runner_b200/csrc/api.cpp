@@ -1,0 +1,394 @@
+// api.cpp - the C ABI: validation, error latch, resident weights, dispatch.
+//
+// Validation restates what the reference relies on before the arithmetic
+// runs: MLX's quantized_matmul shape rules for the two microscaling modes
+// (packed U32 [N, K*bits/32], U8 scales [N, K/group], transpose=true, no
+// biases; src/model.zig:244-258) and the loader's spec rules
+// (src/weights.zig:132-185, in spec.cpp).  Every failure returns a status
+// and latches a message (src/mlx.zig:719-805); nothing calls exit().
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <atomic>
+#include <vector>
+
+#include "internal.h"
+
+namespace qmm {
+namespace {
+
+std::mutex g_err_mu;
+int g_err_status = QMM_OK;
+char g_err_msg[512] = {0};
+std::atomic<bool> g_err_latched{false};
+
+std::atomic<uint64_t> g_fault_remaining{0};
+std::atomic<bool> g_fault_fired{false};
+
+std::mutex g_dev_mu;
+std::vector<DeviceInfo> g_dev_info;
+std::vector<bool> g_dev_known;
+
+}  // namespace
+
+int set_error(int status, const char* fmt, ...) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    if (!g_err_latched.load(std::memory_order_acquire)) {
+        va_list ap;
+        va_start(ap, fmt);
+        std::vsnprintf(g_err_msg, sizeof(g_err_msg), fmt, ap);
+        va_end(ap);
+        g_err_status = status;
+        g_err_latched.store(true, std::memory_order_release);
+    }
+    return status;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    const int st = (e == cudaErrorMemoryAllocation) ? QMM_ERR_OUT_OF_MEMORY : QMM_ERR_CUDA;
+    return set_error(st, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool fault_hit() {
+    uint64_t cur = g_fault_remaining.load();
+    while (cur != 0) {
+        if (g_fault_remaining.compare_exchange_weak(cur, cur - 1)) {
+            if (cur == 1) {
+                g_fault_fired.store(true);
+                return true;
+            }
+            return false;
+        }
+    }
+    return false;
+}
+
+int device_info(int device, DeviceInfo* out) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (device < 0) return set_error(QMM_ERR_BAD_ARGUMENT, "bad device %d", device);
+    if ((size_t)device >= g_dev_info.size()) {
+        g_dev_info.resize(device + 1);
+        g_dev_known.resize(device + 1, false);
+    }
+    if (!g_dev_known[device]) {
+        DeviceInfo d;
+        QMM_CUDA_TRY(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device));
+        QMM_CUDA_TRY(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, device));
+        QMM_CUDA_TRY(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, device));
+        int optin = 0;
+        QMM_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+        d.smem_optin = (size_t)optin;
+        g_dev_info[device] = d;
+        g_dev_known[device] = true;
+    }
+    *out = g_dev_info[device];
+    if (out->major != 10 || out->minor != 0)
+        return set_error(QMM_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only",
+                         device, out->major, out->minor);
+    return QMM_OK;
+}
+
+int dispatch(const QmmArgs& a, cudaStream_t stream) {
+    if (a.m == 0 || a.n == 0) return QMM_OK;
+    if (a.m <= gemv_max_m()) return launch_gemv(a, stream);
+    bool handled = false;
+    if (!a.yf) {
+        if (int rc = launch_gemm(a, stream, &handled)) return rc;
+        if (handled) return QMM_OK;
+    }
+    // Shapes outside the GEMM kernel's envelope: row blocks of the GEMV.
+    for (int64_t m0 = 0; m0 < a.m; m0 += gemv_max_m()) {
+        QmmArgs b = a;
+        b.m = std::min<int64_t>(gemv_max_m(), a.m - m0);
+        b.x = a.x + m0 * a.ldx;
+        if (a.yf) b.yf = a.yf + m0 * a.ldy;
+        else b.y = a.y + m0 * a.ldy;
+        if (int rc = launch_gemv(b, stream)) return rc;
+    }
+    return QMM_OK;
+}
+
+namespace {
+
+// Shared checks of x / y against a validated weight geometry.
+int check_xy(const void* x, int64_t m, int64_t k, int64_t ldx, const void* y, int64_t n, int64_t ldy) {
+    if (m < 0) return set_error(QMM_ERR_BAD_SHAPE, "m=%lld < 0", (long long)m);
+    if (m == 0 || n == 0) return QMM_OK;
+    if (!x || !y) return set_error(QMM_ERR_BAD_ARGUMENT, "x or y is NULL");
+    if (ldx < k) return set_error(QMM_ERR_BAD_SHAPE, "ldx=%lld < k=%lld", (long long)ldx, (long long)k);
+    if (ldy < n) return set_error(QMM_ERR_BAD_SHAPE, "ldy=%lld < n=%lld", (long long)ldy, (long long)n);
+    if ((reinterpret_cast<uintptr_t>(x) & 3) || (ldx & 1))
+        return set_error(QMM_ERR_BAD_ARGUMENT, "x must be 4-byte aligned with an even row stride");
+    if (reinterpret_cast<uintptr_t>(y) & 1) return set_error(QMM_ERR_BAD_ARGUMENT, "y is not 2-byte aligned");
+    return QMM_OK;
+}
+
+int current_device(int* dev) {
+    QMM_CUDA_TRY(cudaGetDevice(dev));
+    DeviceInfo info;
+    return device_info(*dev, &info);
+}
+
+}  // namespace
+}  // namespace qmm
+
+using namespace qmm;
+
+extern "C" int qmm_abi_version(void) { return QMM_ABI_VERSION; }
+
+extern "C" int qmm_last_error(char* buf, size_t len) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    const int st = g_err_latched.load() ? g_err_status : QMM_OK;
+    if (buf && len) {
+        if (g_err_latched.load()) std::snprintf(buf, len, "%s", g_err_msg);
+        else buf[0] = 0;
+    }
+    g_err_latched.store(false);
+    g_err_status = QMM_OK;
+    g_err_msg[0] = 0;
+    return st;
+}
+
+extern "C" int qmm_error_pending(void) { return g_err_latched.load() ? 1 : 0; }
+
+extern "C" int qmm_fault_arm(uint64_t k) {
+    g_fault_fired.store(false);
+    g_fault_remaining.store(k);
+    return QMM_OK;
+}
+
+extern "C" int qmm_fault_fired(void) { return g_fault_fired.load() ? 1 : 0; }
+
+#define QMM_FAULT_POINT(name)                                                   \
+    do {                                                                        \
+        if (::qmm::fault_hit())                                                 \
+            return ::qmm::set_error(QMM_ERR_INJECTED, "%s: injected failure", name); \
+    } while (0)
+
+extern "C" int qmm_quantized_matmul(void* y_dev, int64_t ldy, const void* x_dev, int64_t m, int64_t k,
+                                    int64_t ldx, const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
+                                    const uint8_t* scales_dev, int64_t s_rows, int64_t s_cols,
+                                    const void* biases, bool transpose, qmm_optional_int group_size,
+                                    qmm_optional_int bits, const char* mode, void* stream) {
+    QMM_FAULT_POINT("qmm_quantized_matmul");
+    qmm_quant_spec spec;
+    if (int rc = qmm_spec_from_args(group_size, bits, mode, &spec)) return rc;
+    if (biases) return set_error(QMM_ERR_BAD_ARGUMENT, "%s takes no biases", mode);
+    if (!transpose) return set_error(QMM_ERR_BAD_ARGUMENT, "only transpose=true (W [N, K]) is supported");
+    if (k <= 0 || k % spec.group_size)
+        return set_error(QMM_ERR_BAD_SHAPE, "k=%lld is not a positive multiple of group %d", (long long)k, spec.group_size);
+    if (w_rows < 0 || w_rows != s_rows)
+        return set_error(QMM_ERR_BAD_SHAPE, "w rows %lld != scales rows %lld", (long long)w_rows, (long long)s_rows);
+    if (w_cols * 32 / spec.bits != k || (w_cols * 32) % spec.bits)
+        return set_error(QMM_ERR_BAD_SHAPE, "w cols %lld do not pack k=%lld at %d bits", (long long)w_cols,
+                         (long long)k, spec.bits);
+    if (s_cols * spec.group_size != k)
+        return set_error(QMM_ERR_BAD_SHAPE, "scales cols %lld != k/group = %lld", (long long)s_cols,
+                         (long long)(k / spec.group_size));
+    const int64_t n = w_rows;
+    if (int rc = check_xy(x_dev, m, k, ldx, y_dev, n, ldy)) return rc;
+    if (m == 0 || n == 0) return QMM_OK;
+    if (!w_dev || !scales_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "w or scales is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    QmmArgs a;
+    a.fmt = format_of(spec);
+    a.codes = reinterpret_cast<const uint8_t*>(w_dev);
+    a.ldc = w_cols * 4;
+    a.scales = scales_dev;
+    a.lds = s_cols;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(y_dev);
+    a.ldy = ldy;
+    a.m = m; a.n = n; a.k = k;
+    return dispatch(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t n, int64_t k, int64_t ldw,
+                                 int64_t lds, qmm_quant_spec spec, int src_kind, void* stream,
+                                 qmm_weight** out) {
+    QMM_FAULT_POINT("qmm_weight_create");
+    if (!out) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (int rc = check_spec(spec)) return rc;
+    if (n < 0 || k <= 0 || k % spec.group_size)
+        return set_error(QMM_ERR_BAD_SHAPE, "bad weight shape [%lld, %lld] for group %d", (long long)n, (long long)k,
+                         spec.group_size);
+    if (src_kind != QMM_SRC_HOST && src_kind != QMM_SRC_DEVICE)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "src_kind %d", src_kind);
+    const int64_t row_bytes = k * spec.bits / 8, ngroups = k / spec.group_size;
+    if (ldw == 0) ldw = row_bytes;
+    if (lds == 0) lds = ngroups;
+    if (ldw < row_bytes || lds < ngroups) return set_error(QMM_ERR_BAD_SHAPE, "source row stride too small");
+    if (n > 0 && (!codes || !scales)) return set_error(QMM_ERR_BAD_ARGUMENT, "codes or scales is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    qmm_weight* w = new qmm_weight();
+    w->device = dev;
+    w->n = n;
+    w->k = k;
+    w->spec = spec;
+    w->ldc = (row_bytes + 15) / 16 * 16;  // 16-byte rows for vector loads
+    w->lds = ngroups;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaMemcpyKind kind = src_kind == QMM_SRC_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    auto fail = [&](cudaError_t e, const char* what) {
+        const int rc = cuda_error(e, what);
+        cudaFree(w->codes);
+        cudaFree(w->scales);
+        delete w;
+        return rc;
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&w->codes, (size_t)std::max<int64_t>(1, w->ldc * n))) != cudaSuccess) return fail(e, "cudaMalloc(codes)");
+    if ((e = cudaMalloc(&w->scales, (size_t)std::max<int64_t>(1, w->lds * n))) != cudaSuccess) return fail(e, "cudaMalloc(scales)");
+    if (n > 0) {
+        if (w->ldc != row_bytes && (e = cudaMemsetAsync(w->codes, 0, (size_t)(w->ldc * n), s)) != cudaSuccess)
+            return fail(e, "cudaMemsetAsync(codes)");
+        if ((e = cudaMemcpy2DAsync(w->codes, w->ldc, codes, ldw, row_bytes, n, kind, s)) != cudaSuccess)
+            return fail(e, "copy codes");
+        if ((e = cudaMemcpy2DAsync(w->scales, w->lds, scales, lds, ngroups, n, kind, s)) != cudaSuccess)
+            return fail(e, "copy scales");
+    }
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return fail(e, "cudaStreamSynchronize");
+    *out = w;
+    return QMM_OK;
+}
+
+extern "C" int qmm_shard_range(int64_t n_full, int64_t k_full, qmm_quant_spec spec, int axis, int rank,
+                               int nranks, int64_t* row0, int64_t* rows, int64_t* col0, int64_t* cols) {
+    if (int rc = check_spec(spec)) return rc;
+    if (!row0 || !rows || !col0 || !cols) return set_error(QMM_ERR_BAD_ARGUMENT, "null output");
+    if (nranks < 1 || rank < 0 || rank >= nranks)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "rank %d of %d", rank, nranks);
+    if (n_full < 0 || k_full <= 0 || k_full % spec.group_size)
+        return set_error(QMM_ERR_BAD_SHAPE, "bad full weight shape [%lld, %lld]", (long long)n_full,
+                         (long long)k_full);
+    if (axis == 0) {
+        // Column-parallel: contiguous row blocks, sizes differing by at most one.
+        const int64_t r0 = n_full * rank / nranks, r1 = n_full * (rank + 1) / nranks;
+        *row0 = r0; *rows = r1 - r0; *col0 = 0; *cols = k_full;
+        return QMM_OK;
+    }
+    if (axis != 1) return set_error(QMM_ERR_BAD_ARGUMENT, "axis %d (0 = rows/N, 1 = columns/K)", axis);
+    // Row-parallel: equal K slices that start on a group boundary and on a
+    // whole U32 word.
+    const int64_t unit = std::max<int64_t>(spec.group_size, 32 / spec.bits);
+    if (k_full % nranks || (k_full / nranks) % unit)
+        return set_error(QMM_ERR_BAD_SHAPE, "k=%lld does not split into %d shards of whole groups/words",
+                         (long long)k_full, nranks);
+    *row0 = 0; *rows = n_full; *cols = k_full / nranks; *col0 = *cols * rank;
+    return QMM_OK;
+}
+
+extern "C" int qmm_weight_create_shard(const void* codes, const void* scales, int64_t n_full, int64_t k_full,
+                                       qmm_quant_spec spec, int src_kind, int axis, int rank, int nranks,
+                                       void* stream, qmm_weight** out) {
+    int64_t r0, rows, c0, cols;
+    if (int rc = qmm_shard_range(n_full, k_full, spec, axis, rank, nranks, &r0, &rows, &c0, &cols)) return rc;
+    const int64_t row_bytes = k_full * spec.bits / 8, ngroups = k_full / spec.group_size;
+    const uint8_t* c = static_cast<const uint8_t*>(codes);
+    const uint8_t* sc = static_cast<const uint8_t*>(scales);
+    return qmm_weight_create(c ? c + r0 * row_bytes + c0 * spec.bits / 8 : nullptr,
+                             sc ? sc + r0 * ngroups + c0 / spec.group_size : nullptr, rows, cols, row_bytes,
+                             ngroups, spec, src_kind, stream, out);
+}
+
+extern "C" int qmm_weight_destroy(qmm_weight* w) {
+    if (!w) return QMM_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (w->device >= 0) cudaSetDevice(w->device);
+    cudaError_t e1 = cudaFree(w->codes);
+    cudaError_t e2 = cudaFree(w->scales);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete w;
+    if (e1 != cudaSuccess) return cuda_error(e1, "cudaFree(codes)");
+    if (e2 != cudaSuccess) return cuda_error(e2, "cudaFree(scales)");
+    return QMM_OK;
+}
+
+extern "C" int qmm_weight_info(const qmm_weight* w, int64_t* n, int64_t* k, qmm_quant_spec* spec, int* device) {
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    if (spec) *spec = w->spec;
+    if (device) *device = w->device;
+    return QMM_OK;
+}
+
+namespace {
+
+int weight_args(const qmm_weight* w, QmmArgs* a) {
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (dev != w->device)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "weight lives on device %d, current device is %d", w->device, dev);
+    a->fmt = format_of(w->spec);
+    a->codes = w->codes;
+    a->ldc = w->ldc;
+    a->scales = w->scales;
+    a->lds = w->lds;
+    a->n = w->n;
+    a->k = w->k;
+    return QMM_OK;
+}
+
+}  // namespace
+
+extern "C" int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* y_dev, int64_t ldy,
+                       bool transpose, void* stream) {
+    QMM_FAULT_POINT("qmm_run");
+    if (!transpose) return set_error(QMM_ERR_BAD_ARGUMENT, "only transpose=true (W [N, K]) is supported");
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (int rc = check_xy(x_dev, m, w->k, ldx, y_dev, w->n, ldy)) return rc;
+    if (m == 0 || w->n == 0) return QMM_OK;
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(y_dev);
+    a.ldy = ldy;
+    a.m = m;
+    return dispatch(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m, int64_t ldx,
+                          void* y_dev, int64_t ldy, void* stream) {
+    // src/model.zig:226-228: a packed U32 weight without scales is MissingWeight.
+    if (!w && has_packed_u32) return set_error(QMM_ERR_MISSING_WEIGHT, "packed weight has no scales");
+    if (!w) return set_error(QMM_ERR_MISSING_WEIGHT, "weight is missing");
+    return qmm_run(w, x_dev, m, ldx, y_dev, ldy, true, stream);
+}
+
+extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dtype, void* stream) {
+    QMM_FAULT_POINT("qmm_dequantize");
+    if (out_dtype != QMM_DTYPE_BF16 && out_dtype != QMM_DTYPE_F32)
+        return set_error(QMM_ERR_UNSUPPORTED_DTYPE, "dequantize output dtype %d (BF16 or F32)", out_dtype);
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    if (w->n == 0) return QMM_OK;
+    if (!out_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
+    return launch_dequant(a.fmt, a.codes, a.ldc, a.scales, a.lds, a.n, a.k, out_dev, out_dtype == QMM_DTYPE_BF16,
+                          static_cast<cudaStream_t>(stream));
+}
+
+// Used by tp.cpp: the row-parallel partial product in fp32.
+namespace qmm {
+int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, float* yf, int64_t ldy,
+                    cudaStream_t stream) {
+    if (int rc = check_xy(x_dev, m, w ? w->k : 0, ldx, yf, w ? w->n : 0, ldy)) return rc;
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = nullptr;
+    a.yf = yf;
+    a.ldy = ldy;
+    a.m = m;
+    return dispatch(a, stream);
+}
+}  // namespace qmm

@@ -1,0 +1,87 @@
+// internal.h - host-side declarations shared by the library's translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/qmm.h"
+
+namespace qmm {
+
+// ---- error latch (src/mlx.zig:719-805 restated for a C ABI) --------------
+// The first failure since the last qmm_last_error() wins; later ones are
+// dropped so follow-on noise cannot hide the cause.  Returns `status`.
+int set_error(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Translate a CUDA error into QMM_ERR_CUDA / QMM_ERR_OUT_OF_MEMORY + latch.
+int cuda_error(cudaError_t e, const char* what);
+// The fault-injection hook: true when the armed k-th checked call is this one.
+bool fault_hit();
+
+#define QMM_CUDA_TRY(expr)                                            \
+    do {                                                              \
+        cudaError_t _e = (expr);                                      \
+        if (_e != cudaSuccess) return ::qmm::cuda_error(_e, #expr);   \
+    } while (0)
+
+// ---- formats ----------------------------------------------------------------
+enum Format : int { kMXFP8 = 0, kNVFP4 = 1 };
+
+inline int format_of(const qmm_quant_spec& s) { return s.mode == QMM_MODE_MXFP8 ? kMXFP8 : kNVFP4; }
+// Validates (mode, group, bits) against the two supported pairs.
+int check_spec(const qmm_quant_spec& s);
+
+// Device properties cached per device (SM count, compute capability).
+struct DeviceInfo {
+    int sms = 0;
+    int major = 0, minor = 0;
+    size_t smem_optin = 0;
+};
+int device_info(int device, DeviceInfo* out);
+
+// ---- kernels -----------------------------------------------------------------
+// Operands of one y = x . dequant(W)^T call, all device pointers.
+struct QmmArgs {
+    int fmt;                 // Format
+    const uint8_t* codes;    // [n][ldc] bytes, K*bits/8 meaningful per row
+    int64_t ldc;             // bytes between code rows
+    const uint8_t* scales;   // [n][lds] bytes, K/group per row
+    int64_t lds;
+    const uint16_t* x;       // bf16 [m][ldx]
+    int64_t ldx;             // elements
+    uint16_t* y;             // bf16 [m][ldy]
+    int64_t ldy;             // elements
+    float* yf = nullptr;     // when set: fp32 output [m][ldy] instead of y
+    int64_t m, n, k;
+};
+
+// Split-K GEMV for m <= 8 (decode / MTP verify).  No workspace: the split-K
+// partials are reduced through distributed shared memory inside a cluster.
+int launch_gemv(const QmmArgs& a, cudaStream_t stream);
+int gemv_max_m();
+
+// Dequantize W into out[n][k] (bf16 if out_bf16 else fp32), row stride k.
+int launch_dequant(int fmt, const uint8_t* codes, int64_t ldc, const uint8_t* scales,
+                   int64_t lds, int64_t n, int64_t k, void* out, bool out_bf16,
+                   cudaStream_t stream);
+
+// Prefill GEMM (m > 8) on the tcgen05 tensor cores.  Returns QMM_OK or an
+// error; *handled = false when the shape is outside the kernel's envelope
+// (the caller then uses the GEMV path over row blocks).
+int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled);
+
+// Route one call to the right kernel family.
+int dispatch(const QmmArgs& a, cudaStream_t stream);
+
+}  // namespace qmm
+
+// Resident weight (opaque in the C ABI).
+struct qmm_weight {
+    int device = -1;
+    int64_t n = 0, k = 0;
+    qmm_quant_spec spec{};
+    uint8_t* codes = nullptr;   // device, row stride ldc (multiple of 16 bytes)
+    int64_t ldc = 0;
+    uint8_t* scales = nullptr;  // device, row stride lds
+    int64_t lds = 0;
+};

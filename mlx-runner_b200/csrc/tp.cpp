@@ -1,0 +1,171 @@
+// tp.cpp - tensor-parallel plumbing: NCCL communicator + row-parallel run.
+//
+// The reference has no distributed backend (--tp is parsed and logged as a
+// single-device stub, src/main.zig:210-215, :338-340); the sharding here is
+// the one the qmm path needs.  Column-parallel (N) shards need no exchange.
+// Row-parallel (K) shards produce partial sums that are added across ranks:
+// the partials are kept in fp32 and reduced with one NCCL fp32 all-reduce,
+// then rounded to bf16 once, so the result carries a single bf16 rounding
+// as on one GPU (adding bf16-rounded partials in bf16 measurably exceeds a
+// 2e-3 relative error at 2+ ranks).
+//
+// NCCL is loaded with dlopen on first use (the copy already in the process,
+// e.g. torch's, if any; else $QMM_NCCL_LIBRARY; else libnccl.so.2), so the
+// library itself loads on machines without NCCL.
+#include <dlfcn.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include <nccl.h>
+
+#include "internal.h"
+
+namespace qmm {
+int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, float* yf, int64_t ldy,
+                    cudaStream_t stream);
+int launch_f32_to_bf16(const float* in, int64_t rows, int64_t cols, int64_t ld_in, uint16_t* out, int64_t ld_out,
+                       cudaStream_t stream);
+}  // namespace qmm
+
+struct qmm_comm {
+    ncclComm_t comm = nullptr;
+    int nranks = 0, rank = 0, device = -1;
+    float* partial = nullptr;   // fp32 [capacity] partial sums
+    int64_t capacity = 0;
+};
+
+namespace {
+
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+std::once_flag g_once;
+NcclApi g_api;
+
+void load_nccl() {
+    void* h = nullptr;
+    if (const char* p = std::getenv("QMM_NCCL_LIBRARY")) h = dlopen(p, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    g_api.GetUniqueId = reinterpret_cast<decltype(g_api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    g_api.CommInitRank = reinterpret_cast<decltype(g_api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+    g_api.CommDestroy = reinterpret_cast<decltype(g_api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+    g_api.AllReduce = reinterpret_cast<decltype(g_api.AllReduce)>(dlsym(h, "ncclAllReduce"));
+    g_api.GetErrorString = reinterpret_cast<decltype(g_api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+    g_api.ok = g_api.GetUniqueId && g_api.CommInitRank && g_api.CommDestroy && g_api.AllReduce &&
+               g_api.GetErrorString;
+}
+
+int nccl(int* rc_out) {
+    std::call_once(g_once, load_nccl);
+    if (!g_api.ok) {
+        *rc_out = qmm::set_error(QMM_ERR_NCCL, "NCCL could not be loaded (set QMM_NCCL_LIBRARY)");
+        return 0;
+    }
+    return 1;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+    return qmm::set_error(QMM_ERR_NCCL, "%s: %s", what, g_api.GetErrorString ? g_api.GetErrorString(r) : "?");
+}
+
+}  // namespace
+
+using qmm::set_error;
+
+extern "C" int qmm_tp_unique_id(void* id128) {
+    int rc = QMM_OK;
+    if (!nccl(&rc)) return rc;
+    if (!id128) return set_error(QMM_ERR_BAD_ARGUMENT, "id is NULL");
+    ncclUniqueId id;
+    if (ncclResult_t r = g_api.GetUniqueId(&id)) return nccl_fail(r, "ncclGetUniqueId");
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+    std::memcpy(id128, &id, sizeof(id));
+    return QMM_OK;
+}
+
+extern "C" int qmm_tp_comm_create(const void* id128, int nranks, int rank, int64_t max_partial_elems,
+                                  qmm_comm** out) {
+    if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_comm_create: injected failure");
+    if (!id128 || !out) return set_error(QMM_ERR_BAD_ARGUMENT, "id or out is NULL");
+    *out = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks || max_partial_elems < 0)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "rank %d of %d, capacity %lld", rank, nranks,
+                         (long long)max_partial_elems);
+    int rc = QMM_OK;
+    if (!nccl(&rc)) return rc;
+    qmm_comm* c = new qmm_comm();
+    c->nranks = nranks;
+    c->rank = rank;
+    if (cudaError_t e = cudaGetDevice(&c->device)) {
+        delete c;
+        return qmm::cuda_error(e, "cudaGetDevice");
+    }
+    if (max_partial_elems > 0) {
+        if (cudaError_t e = cudaMalloc(&c->partial, (size_t)max_partial_elems * sizeof(float))) {
+            delete c;
+            return qmm::cuda_error(e, "cudaMalloc(partial)");
+        }
+        c->capacity = max_partial_elems;
+    }
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof(id));
+    if (ncclResult_t r = g_api.CommInitRank(&c->comm, nranks, id, rank)) {
+        cudaFree(c->partial);
+        delete c;
+        return nccl_fail(r, "ncclCommInitRank");
+    }
+    *out = c;
+    return QMM_OK;
+}
+
+extern "C" int qmm_tp_comm_destroy(qmm_comm* c) {
+    if (!c) return QMM_OK;
+    int rc = QMM_OK;
+    if (c->comm && g_api.ok) {
+        if (ncclResult_t r = g_api.CommDestroy(c->comm)) rc = nccl_fail(r, "ncclCommDestroy");
+    }
+    if (c->partial) cudaFree(c->partial);
+    delete c;
+    return rc;
+}
+
+extern "C" int qmm_tp_allreduce_bf16(qmm_comm* c, void* buf_dev, int64_t count, void* stream) {
+    if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_allreduce_bf16: injected failure");
+    if (!c) return set_error(QMM_ERR_BAD_ARGUMENT, "comm is NULL");
+    if (count < 0 || (count > 0 && !buf_dev)) return set_error(QMM_ERR_BAD_ARGUMENT, "bad buffer");
+    if (ncclResult_t r = g_api.AllReduce(buf_dev, buf_dev, (size_t)count, ncclBfloat16, ncclSum, c->comm,
+                                         static_cast<cudaStream_t>(stream)))
+        return nccl_fail(r, "ncclAllReduce(bf16)");
+    return QMM_OK;
+}
+
+extern "C" int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const void* x_dev, int64_t m, int64_t ldx,
+                                      void* y_dev, int64_t ldy, void* stream) {
+    if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_run_rowparallel: injected failure");
+    if (!c || !w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight or comm is NULL");
+    int64_t n = 0, k = 0;
+    qmm_weight_info(w, &n, &k, nullptr, nullptr);
+    if (m < 0) return set_error(QMM_ERR_BAD_SHAPE, "m < 0");
+    if (m * n > c->capacity)
+        return set_error(QMM_ERR_BAD_SHAPE, "m*n=%lld exceeds the communicator's partial buffer (%lld)",
+                         (long long)(m * n), (long long)c->capacity);
+    if (ldy < n) return set_error(QMM_ERR_BAD_SHAPE, "ldy < n");
+    if (m == 0 || n == 0) return QMM_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (int rc = qmm::run_partial_f32(w, x_dev, m, ldx, c->partial, n, s)) return rc;
+    if (ncclResult_t r = g_api.AllReduce(c->partial, c->partial, (size_t)(m * n), ncclFloat32, ncclSum, c->comm, s))
+        return nccl_fail(r, "ncclAllReduce(f32)");
+    return qmm::launch_f32_to_bf16(c->partial, m, n, n, static_cast<uint16_t*>(y_dev), ldy, s);
+}

@@ -1,0 +1,371 @@
+"""Python binding of libqmm_b200.so - the operator surface of mlx-runner's
+quantized linear layer, on B200.
+
+Mirrors the reference's interface for this path:
+  * ``quantized_matmul(x, w, scales, biases=None, transpose=True,
+    group_size=None, bits=None, mode=...)``  ->  mlx_quantized_matmul
+    (src/mlx.zig:265, called by qlinear src/model.zig:244-258);
+  * ``infer_quant_spec(tensors)``  ->  inferQuantSpec (src/weights.zig:132-185);
+  * ``QuantizedWeight``  ->  a resident packed weight as WeightMap holds it
+    (src/weights.zig:203-353), run like namedLinearQ / qlinear;
+  * ``QmmError``  ->  the error latch (src/mlx.zig:719-805), raised with the
+    reference's error class names.
+
+The arithmetic runs only in the CUDA library: importing this module without
+the built library, or calling it without a B200, raises - there is no CPU
+fallback.  torch tensors are used purely as device buffers and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Iterable, Optional, Sequence
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libqmm_b200.so")
+
+QMM_OK = 0
+STATUS_NAMES = {
+    1: "BadShape", 2: "NonstandardQuant", 3: "InconsistentQuant", 4: "AffineUnsupported",
+    5: "UnsupportedDtype", 6: "BadMode", 7: "BadArgument", 8: "MissingWeight",
+    20: "CudaError", 21: "OutOfMemory", 22: "NcclError", 23: "Timeout", 24: "NoDevice",
+    30: "Injected",
+}
+MODE_NONE, MODE_MXFP8, MODE_NVFP4 = 0, 1, 2
+MODE_NAMES = {MODE_NONE: "none", MODE_MXFP8: "mxfp8", MODE_NVFP4: "nvfp4"}
+DTYPES = {"BF16": 0, "F32": 1, "U32": 2, "U8": 3}
+SRC_HOST, SRC_DEVICE = 0, 1
+
+# Every symbol the C ABI (include/qmm.h) exports.
+EXPORTS = (
+    "qmm_abi_version", "qmm_infer_quant_spec", "qmm_mode_str", "qmm_spec_from_args",
+    "qmm_quantized_matmul", "qmm_weight_create", "qmm_weight_create_shard", "qmm_shard_range",
+    "qmm_weight_destroy",
+    "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
+    "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
+    "qmm_last_error", "qmm_error_pending", "qmm_fault_arm", "qmm_fault_fired",
+)
+
+
+class QmmError(RuntimeError):
+    """A non-zero qmm status; ``name`` is the reference's error class."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        self.name = STATUS_NAMES.get(status, f"Status{status}")
+        super().__init__(f"{self.name}: {message}")
+
+
+class QuantSpec(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int32), ("group_size", ctypes.c_int32), ("bits", ctypes.c_int32)]
+
+    @property
+    def mode_str(self) -> str:
+        return MODE_NAMES.get(self.mode, "?")
+
+    def astuple(self):
+        return (self.mode_str, self.group_size, self.bits)
+
+
+class TensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("ndim", ctypes.c_int32),
+                ("shape", ctypes.POINTER(ctypes.c_int64))]
+
+
+class OptionalInt(ctypes.Structure):
+    _fields_ = [("value", ctypes.c_int), ("has_value", ctypes.c_bool)]
+
+    @classmethod
+    def of(cls, v: Optional[int]) -> "OptionalInt":
+        return cls(0, False) if v is None else cls(int(v), True)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library; raise if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python mlx-runner_b200/build.py`")
+    L = ctypes.CDLL(LIB_PATH)
+    i64, vp, i32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+    L.qmm_infer_quant_spec.argtypes = [ctypes.POINTER(TensorInfo), i64, ctypes.POINTER(QuantSpec)]
+    L.qmm_mode_str.argtypes = [QuantSpec]
+    L.qmm_mode_str.restype = ctypes.c_char_p
+    L.qmm_spec_from_args.argtypes = [OptionalInt, OptionalInt, ctypes.c_char_p, ctypes.POINTER(QuantSpec)]
+    L.qmm_quantized_matmul.argtypes = [vp, i64, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp,
+                                       ctypes.c_bool, OptionalInt, OptionalInt, ctypes.c_char_p, vp]
+    L.qmm_weight_create.argtypes = [vp, vp, i64, i64, i64, i64, QuantSpec, i32, vp, ctypes.POINTER(vp)]
+    L.qmm_weight_create_shard.argtypes = [vp, vp, i64, i64, QuantSpec, i32, i32, i32, i32, vp,
+                                          ctypes.POINTER(vp)]
+    L.qmm_shard_range.argtypes = [i64, i64, QuantSpec, i32, i32, i32] + [ctypes.POINTER(i64)] * 4
+    L.qmm_weight_destroy.argtypes = [vp]
+    L.qmm_weight_info.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(QuantSpec),
+                                  ctypes.POINTER(i32)]
+    L.qmm_run.argtypes = [vp, vp, i64, i64, vp, i64, ctypes.c_bool, vp]
+    L.qmm_linear.argtypes = [vp, ctypes.c_bool, vp, i64, i64, vp, i64, vp]
+    L.qmm_dequantize.argtypes = [vp, vp, ctypes.c_int32, vp]
+    L.qmm_tp_unique_id.argtypes = [vp]
+    L.qmm_tp_comm_create.argtypes = [vp, i32, i32, i64, ctypes.POINTER(vp)]
+    L.qmm_tp_comm_destroy.argtypes = [vp]
+    L.qmm_tp_allreduce_bf16.argtypes = [vp, vp, i64, vp]
+    L.qmm_tp_run_rowparallel.argtypes = [vp, vp, vp, i64, i64, vp, i64, vp]
+    L.qmm_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    L.qmm_fault_arm.argtypes = [ctypes.c_uint64]
+    for name in EXPORTS:
+        fn = getattr(L, name)
+        if name != "qmm_mode_str":
+            fn.restype = ctypes.c_int
+    _lib = L
+    return L
+
+
+def check(rc: int) -> None:
+    """Raise QmmError for a non-zero status (src/mlx.zig:589 check)."""
+    if rc != QMM_OK:
+        buf = ctypes.create_string_buffer(512)
+        lib().qmm_last_error(buf, len(buf))
+        raise QmmError(rc, buf.value.decode(errors="replace"))
+
+
+def take_error() -> tuple[int, str]:
+    buf = ctypes.create_string_buffer(512)
+    st = lib().qmm_last_error(buf, len(buf))
+    return st, buf.value.decode(errors="replace")
+
+
+def fault_arm(k: int) -> None:
+    lib().qmm_fault_arm(k)
+
+
+def fault_fired() -> bool:
+    return bool(lib().qmm_fault_fired())
+
+
+# ---- spec inference ---------------------------------------------------------
+
+def infer_quant_spec(tensors: Iterable) -> tuple[str, int, int]:
+    """(mode, group_size, bits) for a checkpoint's tensor infos.
+
+    ``tensors`` yields (name, dtype, shape) with dtype one of BF16/F32/U32/U8.
+    Raises QmmError(NonstandardQuant / InconsistentQuant / AffineUnsupported)
+    exactly where src/weights.zig:132-185 returns those errors.
+    """
+    items = list(tensors)
+    arr = (TensorInfo * max(1, len(items)))()
+    keep = []
+    for i, (name, dtype, shape) in enumerate(items):
+        shp = (ctypes.c_int64 * max(1, len(shape)))(*shape)
+        keep.append(shp)
+        arr[i] = TensorInfo(name.encode(), DTYPES[dtype], len(shape), shp)
+    spec = QuantSpec()
+    check(lib().qmm_infer_quant_spec(arr, len(items), ctypes.byref(spec)))
+    return spec.astuple()
+
+
+def spec_from_args(group_size: Optional[int], bits: Optional[int], mode: str) -> QuantSpec:
+    spec = QuantSpec()
+    check(lib().qmm_spec_from_args(OptionalInt.of(group_size), OptionalInt.of(bits), mode.encode(),
+                                   ctypes.byref(spec)))
+    return spec
+
+
+def make_spec(mode: str) -> QuantSpec:
+    return spec_from_args(None, None, mode)
+
+
+def shard_range(n_full: int, k_full: int, mode: str, axis: int, rank: int, nranks: int):
+    """(row0, rows, col0, cols) of a tensor-parallel shard (pure host)."""
+    out = [ctypes.c_int64() for _ in range(4)]
+    check(lib().qmm_shard_range(n_full, k_full, make_spec(mode), axis, rank, nranks,
+                                *[ctypes.byref(o) for o in out]))
+    return tuple(o.value for o in out)
+
+
+# ---- torch plumbing -----------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def _stream_handle(stream) -> int:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _as_2d(x):
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2
+
+
+def quantized_matmul(x, w, scales, biases=None, transpose: bool = True, group_size: Optional[int] = None,
+                     bits: Optional[int] = None, mode: str = "mxfp8", stream=None, out=None):
+    """y = x . dequant(w, scales)^T for x bf16 [..., K] on the GPU.
+
+    w: uint32 [N, K*bits/32] and scales: uint8 [N, K/group] CUDA tensors in
+    the checkpoint layout (src/weights.zig:154-161).
+    """
+    torch = _torch()
+    if x.dtype != torch.bfloat16:
+        raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+    x2 = _as_2d(x)
+    n = w.shape[0]
+    m, k = x2.shape
+    y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    check(lib().qmm_quantized_matmul(
+        y.data_ptr(), y.stride(0), x2.data_ptr(), m, k, x2.stride(0),
+        w.data_ptr(), w.shape[0], w.shape[1], scales.data_ptr(), scales.shape[0], scales.shape[1],
+        None if biases is None else biases.data_ptr(), transpose, OptionalInt.of(group_size),
+        OptionalInt.of(bits), mode.encode(), _stream_handle(stream)))
+    return y.reshape(*x.shape[:-1], n) if out is None else y
+
+
+@dataclass
+class _Src:
+    ptr: int
+    kind: int
+    keep: object
+
+
+def _src(a, dtype_name: str) -> _Src:
+    """Host numpy array or torch tensor (CPU or CUDA) -> pointer + kind."""
+    torch = _torch()
+    if isinstance(a, torch.Tensor):
+        a = a.contiguous()
+        return _Src(a.data_ptr(), SRC_DEVICE if a.is_cuda else SRC_HOST, a)
+    import numpy as np
+    arr = np.ascontiguousarray(a)
+    return _Src(arr.ctypes.data, SRC_HOST, arr)
+
+
+class QuantizedWeight:
+    """A packed weight resident on the current CUDA device.
+
+    Created from the checkpoint tensors (U32 codes [N, K*bits/32], U8 scales
+    [N, K/group]); the codes are uploaded bit for bit.
+    """
+
+    def __init__(self, codes, scales, mode: str, stream=None, shard: Optional[tuple[int, int, int]] = None):
+        self.spec = make_spec(mode)
+        c, s = _src(codes, "U32"), _src(scales, "U8")
+        n_full = int(codes.shape[0])
+        k_full = int(codes.shape[1]) * 32 // self.spec.bits
+        h = ctypes.c_void_p()
+        if shard is None:
+            check(lib().qmm_weight_create(c.ptr, s.ptr, n_full, k_full, 0, 0, self.spec, c.kind,
+                                          _stream_handle(stream), ctypes.byref(h)))
+        else:
+            axis, rank, nranks = shard
+            check(lib().qmm_weight_create_shard(c.ptr, s.ptr, n_full, k_full, self.spec, c.kind, axis, rank,
+                                                nranks, _stream_handle(stream), ctypes.byref(h)))
+        self._h = h
+        n, k, dev = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        check(lib().qmm_weight_info(h, ctypes.byref(n), ctypes.byref(k), None, ctypes.byref(dev)))
+        self.n, self.k, self.device = n.value, k.value, dev.value
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise QmmError(7, "weight was destroyed")
+        return self._h
+
+    @property
+    def mode(self) -> str:
+        return self.spec.mode_str
+
+    def __call__(self, x, out=None, stream=None):
+        return self.run(x, out=out, stream=stream)
+
+    def run(self, x, out=None, stream=None):
+        torch = _torch()
+        if x.dtype != torch.bfloat16:
+            raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        x2 = _as_2d(x)
+        m = x2.shape[0]
+        y = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
+        check(lib().qmm_run(self.handle, x2.data_ptr(), m, x2.stride(0), y.data_ptr(), y.stride(0), True,
+                            _stream_handle(stream)))
+        return y.reshape(*x.shape[:-1], self.n) if out is None else y
+
+    def dequantize(self, dtype=None, stream=None):
+        torch = _torch()
+        dtype = dtype or torch.bfloat16
+        code = {torch.bfloat16: DTYPES["BF16"], torch.float32: DTYPES["F32"]}[dtype]
+        out = torch.empty((self.n, self.k), dtype=dtype, device=f"cuda:{self.device}")
+        check(lib().qmm_dequantize(self.handle, out.data_ptr(), code, _stream_handle(stream)))
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            check(lib().qmm_weight_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def linear(weight: Optional[QuantizedWeight], x, has_packed_u32: bool = True, out=None, stream=None):
+    """namedLinearQ (src/model.zig:218-233) for one projection."""
+    torch = _torch()
+    x2 = _as_2d(x)
+    if weight is None:
+        check(lib().qmm_linear(None, has_packed_u32, x2.data_ptr(), x2.shape[0], x2.stride(0), None, 0,
+                               _stream_handle(stream)))
+    y = out if out is not None else torch.empty((x2.shape[0], weight.n), dtype=torch.bfloat16, device=x.device)
+    check(lib().qmm_linear(weight.handle, has_packed_u32, x2.data_ptr(), x2.shape[0], x2.stride(0),
+                           y.data_ptr(), y.stride(0), _stream_handle(stream)))
+    return y
+
+
+class TPComm:
+    """NCCL communicator for row-parallel shards (one per rank / GPU)."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, max_partial_elems: int):
+        buf = ctypes.create_string_buffer(bytes(unique_id), 128)
+        h = ctypes.c_void_p()
+        check(lib().qmm_tp_comm_create(buf, nranks, rank, max_partial_elems, ctypes.byref(h)))
+        self._h = h
+        self.nranks, self.rank = nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(lib().qmm_tp_unique_id(buf))
+        return buf.raw
+
+    def run_rowparallel(self, weight: QuantizedWeight, x_shard, out=None, stream=None):
+        torch = _torch()
+        x2 = _as_2d(x_shard)
+        y = out if out is not None else torch.empty((x2.shape[0], weight.n), dtype=torch.bfloat16,
+                                                    device=x_shard.device)
+        check(lib().qmm_tp_run_rowparallel(weight.handle, self._h, x2.data_ptr(), x2.shape[0], x2.stride(0),
+                                           y.data_ptr(), y.stride(0), _stream_handle(stream)))
+        return y
+
+    def allreduce_bf16(self, buf, stream=None):
+        check(lib().qmm_tp_allreduce_bf16(self._h, buf.data_ptr(), buf.numel(), _stream_handle(stream)))
+        return buf
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            check(lib().qmm_tp_comm_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
