@@ -210,6 +210,13 @@ int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const void* x_dev, 
  * latched status (QMM_OK if none).  src/mlx.zig:792 takeError. */
 int qmm_last_error(char* buf, size_t len);
 
+/* Status of the bounded device-side waits since the last call: QMM_OK, or
+ * QMM_ERR_TIMEOUT if a kernel gave up a wait (it then skipped the rest of its
+ * work and released its resources; the word is cleared).  Synchronizes
+ * `stream`; the reference surfaces asynchronous device failures the same way
+ * at its checkError points (src/mlx.zig:858-866). */
+int qmm_device_status(void* stream);
+
 /* 1 when a failure is latched (src/mlx.zig:778 errorPending). */
 int qmm_error_pending(void);
 

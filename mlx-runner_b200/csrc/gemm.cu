@@ -1,9 +1,546 @@
-// gemm.cu - placeholder until the tcgen05 prefill kernel lands.
+// gemm.cu - prefill quantized GEMM on the sm_100a tensor cores (tcgen05).
+//
+// y[M, N] = x[M, K] . dequant(W)[N, K]^T for M > 8 (prefill chunks, the
+// reference's 2048-token chunks of src/engine.zig:19, :367-382, and whole
+// 32k prompts), W in mxfp8 or nvfp4, x / y bf16, fp32 accumulation.
+//
+// Precision: W is dequantised exactly into bf16 (an E4M3 or E2M1 value
+// times its scale has at most 4 + 0 or 2 + 4 significant bits) and x stays
+// bf16, so every product is exact and the kind::f16 MMA accumulates in
+// fp32 - the same arithmetic as the fp64 oracle up to fp32 summation.
+// (Quantising x to FP8/FP4 for the block-scaled MMA kinds would add
+// 2-10% error per element, far outside the 2e-3 tolerance.)
+//
+// Tile: one CTA per SM (persistent) computes y^T tiles of 128 weight rows x
+// 256 tokens: the dequantised W tile is the MMA's A operand (M = 128), the
+// x tile the B operand (N = 256), so each code is dequantised once per 256
+// tokens.  Warp roles (16 warps):
+//   warp 0      TMA producer: x tiles [256 tokens x 64 k] with 128B swizzle
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16) per 64-wide k-block,
+//               fp32 accumulators in TMEM (2 x 256 columns, double-buffered)
+//   warp 2      TMEM allocator
+//   warps 4-7   epilogue: tcgen05.ld -> bf16 -> y (coalesced 64-byte rows)
+//   warps 8-15  dequant: codes + scales straight from global memory (L2),
+//               decoded with cvt.{e4m3x2,e2m1x2}, written as bf16 into the
+//               A tile in the UMMA K-major SWIZZLE_128B layout
+// Pipelines (mbarriers): S stages of {x tile, W tile}: full_x (TMA bytes),
+// full_w (8 dequant warps), empty (MMA commit); accumulators: tmem_full
+// (MMA commit), tmem_empty (4 epilogue warps).  Every wait is bounded by
+// %globaltimer: a wait that gives up raises the CTA's abort flag and the
+// device error word, and every role then drains its in-flight TMA / MMA work,
+// frees TMEM and returns (the host reads the word with qmm_device_status).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "formats.cuh"
 #include "internal.h"
 
 namespace qmm {
-int launch_gemm(const QmmArgs&, cudaStream_t, bool* handled) {
-    *handled = false;
+
+__device__ unsigned int g_device_error = 0;  // bit 0: a bounded wait timed out
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kBK = 64;                     // k per stage (128 bytes of bf16: one swizzle row)
+constexpr int kTileW = 128;                 // weight rows per tile (MMA M)
+constexpr int kTileT = 256;                 // tokens per tile (MMA N)
+constexpr int kThreads = 512;
+constexpr int kXBytes = kTileT * kBK * 2;   // 32 KB
+constexpr int kWBytes = kTileW * kBK * 2;   // 16 KB
+constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kDequantWarps = 8;
+constexpr int kEpiWarps = 4;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+struct GemmParams {
+    const uint8_t* __restrict__ codes;
+    const uint8_t* __restrict__ scales;
+    uint16_t* __restrict__ y;
+    int64_t ldc, lds, ldy;
+    int m, n, k;
+    int kblocks, w_tiles, num_tiles;
+};
+
+// ---- PTX wrappers --------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity.  False = gave up (the
+// abort flag is raised, by this thread if it timed out).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(b, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(b, parity)) return true;
+        if ((i & 15) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > kTimeoutNs) {
+                *abort_flag = 1;
+                atomicOr(&g_device_error, 1u);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x0, int y0) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(y0), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                    // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;          // SBO
+    d |= (uint64_t)1 << 46;                    // descriptor version
+    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+    return d;
+}
+
+// kind::f16 instruction descriptor: bf16 A/B, fp32 D, K-major A and B.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileT >> 3) << 17) |
+                            ((uint32_t)(kTileW >> 4) << 24);
+
+// ---- dequantisation of one half k-block (32 codes) of one weight row --------------
+struct CodeBuf {
+    uint4 c0, c1;     // fp8: 32 bytes; fp4: c0 = 16 bytes
+    uint32_t s;       // scale byte(s): fp8 one, fp4 two (low byte = first group)
+    int valid;        // codes inside K: 0, 16 or 32
+};
+
+template <int FMT>
+__device__ __forceinline__ CodeBuf load_codes(const GemmParams& p, int row, int kk) {
+    CodeBuf b;
+    b.c0 = make_uint4(0, 0, 0, 0);
+    b.c1 = b.c0;
+    b.s = 0;
+    b.valid = 0;
+    if (row >= p.n || kk >= p.k) return b;
+    b.valid = min(32, p.k - kk);
+    const uint8_t* cp = p.codes + (int64_t)row * p.ldc;
+    const uint8_t* sp = p.scales + (int64_t)row * p.lds;
+    if constexpr (FMT == kMXFP8) {
+        b.c0 = __ldg(reinterpret_cast<const uint4*>(cp + kk));
+        b.c1 = __ldg(reinterpret_cast<const uint4*>(cp + kk + 16));
+        b.s = __ldg(sp + kk / 32);
+    } else {
+        if (b.valid == 32) {
+            b.c0 = __ldg(reinterpret_cast<const uint4*>(cp + kk / 2));
+            b.s = (uint32_t)__ldg(sp + kk / 16) | ((uint32_t)__ldg(sp + kk / 16 + 1) << 8);
+        } else {
+            const uint2 h = __ldg(reinterpret_cast<const uint2*>(cp + kk / 2));
+            b.c0 = make_uint4(h.x, h.y, 0, 0);
+            b.s = __ldg(sp + kk / 16);
+        }
+    }
+    return b;
+}
+
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
+    const float2 f = f16x2_to_float2(h);
+    return f32x2_to_bf16x2(f.x, f.y);
+}
+
+// 32 codes -> 4 chunks of 8 bf16 (as uint4), exact.
+template <int FMT>
+__device__ __forceinline__ void dequant32(const CodeBuf& b, uint4 (&out)[4]) {
+    if constexpr (FMT == kMXFP8) {
+        const float s = ue8m0_to_f32(b.s);
+        const uint32_t w[8] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w, b.c1.x, b.c1.y, b.c1.z, b.c1.w};
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint32_t h[2];
+            e4m3x4_to_f16x2(w[i], h);
+            const float2 a = f16x2_to_float2(h[0]), c = f16x2_to_float2(h[1]);
+            o[2 * i] = f32x2_to_bf16x2(a.x * s, a.y * s);
+            o[2 * i + 1] = f32x2_to_bf16x2(c.x * s, c.y * s);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    } else {
+        // E2M1 x UE4M3 products are exact in f16 (<= 6 significant bits,
+        // magnitudes 2^-10 .. 2688), so the scale is applied with HMUL2.
+        const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)((b.s & 0xFF) * 0x0101u));
+        const uint32_t s1 = e4m3x2_to_f16x2((uint16_t)(((b.s >> 8) & 0xFF) * 0x0101u));
+        const uint32_t w[4] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t h[4];
+            e2m1x8_to_f16x2(w[j], h);
+            const uint32_t s = j < 2 ? s0 : s1;
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                __half2 v = __hmul2(*reinterpret_cast<__half2*>(&h[i]), *reinterpret_cast<const __half2*>(&s));
+                o[i] = f16x2_to_bf16x2(*reinterpret_cast<uint32_t*>(&v));
+            }
+            out[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_x = smem;                                   // kStages x 32 KB
+    uint8_t* smem_w = smem + kStages * kXBytes;               // kStages x 16 KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_w + kStages * kWBytes);
+    uint64_t* full_x = bars;
+    uint64_t* full_w = bars + kStages;
+    uint64_t* empty = bars + 2 * kStages;
+    uint64_t* tmem_full = bars + 3 * kStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1);
+    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&full_w[s], kDequantWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
+                     ::"r"(smem_u32(tmem_base_slot)) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_base_slot;
+
+    const int my_tiles = p.num_tiles > (int)blockIdx.x
+                             ? (p.num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total_kb = my_tiles * p.kblocks;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (x tiles) ----------------
+        if (lane == 0) {
+            int issued_phase[kStages];
+            bool issued[kStages];
+            for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
+            for (int it = 0; it < total_kb; ++it) {
+                const int s = it % kStages;
+                const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
+                const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+                const int kb = it % p.kblocks;
+                const int tok0 = (t / p.w_tiles) * kTileT;
+                mbar_expect_tx(&full_x[s], kXBytes);
+                tma_load_2d(smem_x + s * kXBytes, &xmap, &full_x[s], kb * kBK, tok0);
+                issued[s] = true;
+                issued_phase[s] = (int)ph;
+            }
+            if (!*abort_flag) {
+                // Producer tail: wait until the MMA's last commits to every
+                // stage's empty barrier have landed, so no tensor-core arrive
+                // targets this CTA's shared memory after it exits.
+                for (int it = total_kb; it < total_kb + kStages; ++it) {
+                    if (it < kStages) continue;          // stage never used
+                    const int s = it % kStages;
+                    if (!mbar_wait(&empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) break;
+                }
+            }
+            if (*abort_flag) {
+                // Let every TMA still in flight land before the CTA exits.
+                for (int s = 0; s < kStages; ++s)
+                    if (issued[s]) {
+                        const uint64_t t0 = globaltimer();
+                        while (!mbar_try_wait(&full_x[s], (uint32_t)issued_phase[s]) &&
+                               globaltimer() - t0 < kTimeoutNs) {
+                        }
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int it = 0;
+            bool issued_any = false;
+            for (int lt = 0; lt < my_tiles && !*abort_flag; ++lt) {
+                const int a = lt & 1;
+                const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
+                if (!mbar_wait(&tmem_empty[a], aph ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(a * kTileT);
+                bool ok = true;
+                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+                    if (!mbar_wait(&full_x[s], ph, abort_flag) || !mbar_wait(&full_w[s], ph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t xa = smem_u32(smem_x + s * kXBytes);
+                    const uint32_t wa = smem_u32(smem_w + s * kWBytes);
+#pragma unroll
+                    for (int k16 = 0; k16 < kBK / 16; ++k16) {
+                        mma_bf16(d_tmem, sw128_desc(wa + k16 * 32), sw128_desc(xa + k16 * 32), kIdesc,
+                                 (kb > 0 || k16 > 0) ? 1u : 0u);
+                    }
+                    issued_any = true;
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&tmem_full[a]);
+            }
+            if (*abort_flag && issued_any) {
+                // Wait (bounded) for every MMA issued so far before TMEM is freed.
+                mma_commit(drain);
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
+                }
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- epilogue: TMEM -> bf16 -> y ----------------
+        const int q = warp & 3;                     // TMEM lanes 32q .. 32q + 31
+        for (int lt = 0; lt < my_tiles; ++lt) {
+            const int a = lt & 1;
+            const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
+            if (!mbar_wait(&tmem_full[a], aph, abort_flag)) break;
+            tc_fence_after();
+            const int t = (int)blockIdx.x + lt * (int)gridDim.x;
+            const int w_row = (t % p.w_tiles) * kTileW + q * 32 + lane;
+            const int tok0 = (t / p.w_tiles) * kTileT;
+#pragma unroll 1
+            for (int c = 0; c < kTileT / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kTileT + c * 32), r);
+                if (w_row < p.n) {
+                    uint16_t* yp = p.y + (int64_t)(tok0 + c * 32) * p.ldy + w_row;
+                    const int tmax = min(32, p.m - (tok0 + c * 32));
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < tmax) yp[(int64_t)j * p.ldy] = f32_to_bf16(__uint_as_float(r[j]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[a]);
+        }
+    } else if (warp >= 8) {
+        // ---------------- dequant: codes -> bf16 A tiles ----------------
+        const int dt = threadIdx.x - 8 * 32;        // 0 .. 255
+        const int r = dt & (kTileW - 1);            // row within the tile
+        const int h = dt >> 7;                      // k half: [32h, 32h + 32)
+        auto coords = [&](int it, int* row, int* kk) {
+            const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+            *row = (t % p.w_tiles) * kTileW + r;
+            *kk = (it % p.kblocks) * kBK + 32 * h;
+        };
+        CodeBuf cur{}, n1{};
+        int row, kk;
+        if (total_kb > 0) { coords(0, &row, &kk); cur = load_codes<FMT>(p, row, kk); }
+        if (total_kb > 1) { coords(1, &row, &kk); n1 = load_codes<FMT>(p, row, kk); }
+        // Byte offsets of this thread's 4 swizzled 16-byte chunks in a W tile.
+        const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+        for (int it = 0; it < total_kb; ++it) {
+            CodeBuf n2 = n1;
+            if (it + 2 < total_kb) { coords(it + 2, &row, &kk); n2 = load_codes<FMT>(p, row, kk); }
+            const int s = it % kStages;
+            const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+            uint4 o[4];
+            dequant32<FMT>(cur, o);
+            if (cur.valid < 32) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (8 * j >= cur.valid) o[j] = make_uint4(0, 0, 0, 0);
+            }
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
+            uint8_t* wt = smem_w + s * kWBytes + row_off;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = (4 * h + j) ^ (r & 7);
+                *reinterpret_cast<uint4*>(wt + chunk * 16) = o[j];
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_w[s]);
+            cur = n1;
+            n1 = n2;
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+    }
+}
+
+// ---- host side --------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+template <int FMT>
+int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int grid, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    QMM_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !configured[dev]) {
+        QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kSmemBytes));
+        configured[dev] = true;
+    }
+    (void)a;
+    qmm_gemm_kernel<FMT><<<grid, kThreads, kSmemBytes, stream>>>(map, p);
+    QMM_CUDA_TRY(cudaGetLastError());
     return QMM_OK;
 }
+
+}  // namespace
+
+int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
+    *handled = false;
+    // Envelope: 16-byte aligned x rows for TMA, 16-byte aligned code rows for
+    // the dequant warps' vector loads, 32-bit indices.
+    const auto x_addr = reinterpret_cast<uintptr_t>(a.x);
+    const auto c_addr = reinterpret_cast<uintptr_t>(a.codes);
+    if ((x_addr & 15) || ((a.ldx * 2) & 15) || (c_addr & 15) || (a.ldc & 15)) return QMM_OK;
+    if (a.m > INT32_MAX || a.n > INT32_MAX || a.k > INT32_MAX || a.m < 1) return QMM_OK;
+    auto encode = encode_fn();
+    if (!encode) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    int dev = 0;
+    QMM_CUDA_TRY(cudaGetDevice(&dev));
+    DeviceInfo info;
+    if (int rc = device_info(dev, &info)) return rc;
+    if (info.smem_optin < (size_t)kSmemBytes) return QMM_OK;
+
+    CUtensorMap map;
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTileT};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+
+    GemmParams p;
+    p.codes = a.codes; p.scales = a.scales; p.y = a.y;
+    p.ldc = a.ldc; p.lds = a.lds; p.ldy = a.ldy;
+    p.m = (int)a.m; p.n = (int)a.n; p.k = (int)a.k;
+    p.kblocks = (p.k + kBK - 1) / kBK;
+    p.w_tiles = (p.n + kTileW - 1) / kTileW;
+    const int64_t tiles = (int64_t)p.w_tiles * ((p.m + kTileT - 1) / kTileT);
+    if (tiles > INT32_MAX) return QMM_OK;
+    p.num_tiles = (int)tiles;
+    const int grid = (int)std::min<int64_t>(tiles, info.sms);
+    int rc = a.fmt == kMXFP8 ? launch_fmt<kMXFP8>(a, p, map, grid, stream)
+                             : launch_fmt<kNVFP4>(a, p, map, grid, stream);
+    if (rc == QMM_OK) *handled = true;
+    return rc;
+}
+
 }  // namespace qmm
+
+// Device-side status of bounded waits since the last call: QMM_ERR_TIMEOUT
+// if any kernel gave up a wait (the word is cleared).  Synchronizes `stream`.
+extern "C" int qmm_device_status(void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int v = 0, zero = 0;
+    QMM_CUDA_TRY(cudaMemcpyFromSymbolAsync(&v, qmm::g_device_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s));
+    QMM_CUDA_TRY(cudaStreamSynchronize(s));
+    if (v) {
+        QMM_CUDA_TRY(cudaMemcpyToSymbolAsync(qmm::g_device_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s));
+        QMM_CUDA_TRY(cudaStreamSynchronize(s));
+        return qmm::set_error(QMM_ERR_TIMEOUT, "a device-side wait timed out (flags 0x%x)", v);
+    }
+    return QMM_OK;
+}

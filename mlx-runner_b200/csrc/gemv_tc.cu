@@ -1,0 +1,571 @@
+// gemv_tc.cu - decode / MTP-verify quantized GEMM for M <= 8 on resident
+// weights: TMA-fed, tensor-core (mma.sync f16) math, stream-K balanced.
+//
+// y[m, n] = sum_k x[m, k] * dequant(W)[n, k], M <= 8 (decode M = 1,
+// src/engine.zig:428-455; MTP verify M = 2..3, src/engine.zig:548, :656).
+// The op streams W once and is bound by HBM, so the kernel is shaped around
+// keeping HBM busy with few instructions per code:
+//   - persistent grid (one CTA per SM); the work is (128-row block, K-chunk)
+//     units laid out row-block-major and split evenly across CTAs (stream-K),
+//     so every SM streams the same number of bytes whatever N and K are;
+//   - a producer warp streams each unit's codes with one 2D TMA (128-byte
+//     swizzle), its scales with one bulk copy (from the per-unit scale tiles
+//     made at weight creation) and the x chunk with one 2D TMA, into an
+//     8-stage ring: ~130 KB in flight per SM without spending registers;
+//   - a converter warp turns the x chunk into f16 B fragments after an exact
+//     power-of-two scaling into f16 range (per x row and chunk), so every x
+//     value within 2^29 of the chunk's largest is represented exactly;
+//   - 8 consumer warps own 16 rows each and run mma.sync.m16n8k16 (f16 in,
+//     fp32 accumulate) with the weight codes widened by cvt.f16x2.e2m1x2 /
+//     .e4m3x2 (exact).  nvfp4 scales multiply the f16 codes (E2M1 x UE4M3 is
+//     exact in f16); mxfp8 scales (any power of two) are applied in fp32 to
+//     per-group partial sums;
+//   - rows of a block split between CTAs are summed by the last CTA to
+//     finish them, in CTA order (deterministic), through a small fp32
+//     scratch owned by the weight; the counters are reset by that CTA.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "formats.cuh"
+#include "internal.h"
+
+namespace qmm {
+
+extern __device__ unsigned int g_device_error;
+
+namespace {
+
+constexpr int kRows = 128;                 // rows per unit (8 warps x 16)
+constexpr int kStages = 8;
+constexpr int kCodeBytes = kRows * 128;    // 16 KB: 128 code bytes per row per unit
+constexpr int kXRows = 8;                  // x rows staged per unit (M padded to 8)
+constexpr int kThreads = 320;              // producer, converter, 8 consumers
+constexpr int kConsumers = 8;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+template <int FMT> struct Cfg;
+template <> struct Cfg<kMXFP8> {
+    static constexpr int KC = 128;         // codes per row per unit
+    static constexpr int SB = 4;           // scale bytes per row per unit
+};
+template <> struct Cfg<kNVFP4> {
+    static constexpr int KC = 256;
+    static constexpr int SB = 16;
+};
+
+struct TcParams {
+    const uint8_t* __restrict__ scales_tiled;  // [row_blocks][kchunks][128][SB]
+    uint16_t* __restrict__ y;
+    float* __restrict__ partial;               // [grid][2][128][8]
+    unsigned int* __restrict__ counters;       // [row_blocks]
+    int64_t ldy;
+    int m, n, k;
+    int kchunks, row_blocks, units;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t c) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(c));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try(b, parity)) return true;
+        if ((i & 15) == 0) {
+            if (*abort_flag) return false;
+            if (gtimer() - t0 > kTimeoutNs) {
+                *abort_flag = 1;
+                atomicOr(&g_device_error, 2u);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x0, int y0) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(y0), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+                 "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t e2m1_byte(uint32_t w, int byte) {
+    return e2m1x2_to_f16x2((w >> (8 * byte)) & 0xFFu);
+}
+
+// Physical k (within a unit) of x element e (0..7) of B-fragment slot
+// (step pair jp, lane quad c): see the consumer's A mapping.
+template <int FMT>
+__device__ __forceinline__ int slot_k(int jp, int c, int e) {
+    if constexpr (FMT == kNVFP4) {
+        // super-step ss = jp / 4 covers 128 k; thread c owns 32 of them, and
+        // step j = 2 * (jp % 4) + (e / 4) uses its codes 4j .. 4j + 3.
+        return 128 * (jp >> 2) + 32 * c + 8 * (jp & 3) + e;
+    } else {
+        // step j covers [16j, 16j + 16); thread c owns 16j + 4c .. + 3.
+        const int j = 2 * jp + (e >> 2);
+        return 16 * j + 4 * c + (e & 3);
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
+                                                                   const __grid_constant__ CUtensorMap xmap,
+                                                                   TcParams p) {
+    constexpr int KC = Cfg<FMT>::KC, SB = Cfg<FMT>::SB;
+    constexpr int kScaleBytes = kRows * SB;
+    constexpr int kXRawBytes = kXRows * KC * 2;
+    constexpr int kXfBytes = kXRows * KC * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* s_codes = smem;                                          // kStages x 16 KB (1024-aligned)
+    uint8_t* s_scales = s_codes + kStages * kCodeBytes;               // kStages x kScaleBytes
+    uint8_t* s_xraw = s_scales + kStages * kScaleBytes;               // kStages x kXRawBytes
+    uint8_t* s_xf = s_xraw + kStages * kXRawBytes;                    // kStages x kXfBytes
+    float* s_xs = reinterpret_cast<float*>(s_xf + kStages * kXfBytes);  // kStages x 8
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_xs + kStages * 8);
+    uint64_t* full = bars;
+    uint64_t* xready = bars + kStages;
+    uint64_t* empty = bars + 2 * kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kStages);
+    volatile int* s_last = abort_flag + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int u0 = (int)(((int64_t)p.units * blockIdx.x) / gridDim.x);
+    const int u1 = (int)(((int64_t)p.units * (blockIdx.x + 1)) / gridDim.x);
+    const int nunits = u1 - u0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&xready[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            int last = -1;
+            for (int i = 0; i < nunits; ++i) {
+                const int s = i % kStages;
+                const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
+                const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
+                mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes + kXRawBytes);
+                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 128, rb * kRows);
+                bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)u * kScaleBytes, kScaleBytes, &full[s]);
+                tma_2d(s_xraw + s * kXRawBytes, &xmap, &full[s], kc * KC, 0);
+                last = i;
+            }
+            // Drain: every stage's last fill must land, and every consumer
+            // must be done, before the CTA can exit.
+            for (int i = max(0, last - kStages + 1); i <= last; ++i) {
+                const uint64_t t0 = gtimer();
+                while (!mbar_try(&full[i % kStages], (uint32_t)(i / kStages) & 1u) && gtimer() - t0 < kTimeoutNs) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- x converter ----------------
+        for (int i = 0; i < nunits; ++i) {
+            const int s = i % kStages;
+            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            if (!mbar_wait(&full[s], ph, abort_flag)) break;
+            const uint16_t* raw = reinterpret_cast<const uint16_t*>(s_xraw + s * kXRawBytes);
+            float* xs = s_xs + s * 8;
+            // Per x row: amax over the chunk -> exponent e, x scaled by 2^-e
+            // into [2^14, 2^15) before the f16 conversion.
+            float inv[kXRows];
+#pragma unroll
+            for (int m = 0; m < kXRows; ++m) {
+                float a = 0.f;
+                if (m < p.m) {
+                    for (int e = lane; e < KC; e += 32) a = fmaxf(a, fabsf(__uint_as_float((uint32_t)raw[m * KC + e] << 16)));
+#pragma unroll
+                    for (int off = 16; off; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, off));
+                }
+                int ex = 0;
+                if (a > 0.f && a == a) {
+                    ex = (int)((__float_as_uint(a) >> 23) & 0xFF) - 127 - 14;
+                    ex = max(-100, min(100, ex));
+                }
+                inv[m] = __uint_as_float((uint32_t)(127 - ex) << 23);
+                if (lane == 0) xs[m] = __uint_as_float((uint32_t)(127 + ex) << 23);
+            }
+            // B-fragment slots: slot = jp * 32 + (4 * g + c) holds 8 f16 of x row g.
+            uint8_t* xf = s_xf + s * kXfBytes;
+            constexpr int kSlots = KC / 32 * 32;   // (KC / 16 / 2) step pairs x 32 lanes
+            for (int slot = lane; slot < kSlots; slot += 32) {
+                const int jp = slot >> 5, q = slot & 31, g = q >> 2, c = q & 3;
+                uint32_t h[4] = {0, 0, 0, 0};
+                if (g < p.m) {
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        const float v0 = __uint_as_float((uint32_t)raw[g * KC + slot_k<FMT>(jp, c, e)] << 16) * inv[g];
+                        const float v1 = __uint_as_float((uint32_t)raw[g * KC + slot_k<FMT>(jp, c, e + 1)] << 16) * inv[g];
+                        __half2 hv = __floats2half2_rn(v0, v1);
+                        h[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
+                    }
+                }
+                *reinterpret_cast<uint4*>(xf + slot * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xready[s]);
+        }
+    } else {
+        // ---------------- consumers ----------------
+        const int cw = warp - 2;                 // rows [16 cw, 16 cw + 16) of the block
+        const int g = lane >> 2, c = lane & 3;
+        const int r0 = 16 * cw + g, r1 = r0 + 8;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
+        auto flush = [&](int rb, bool complete) {
+            // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.
+            if (complete) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
+                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                }
+                return;
+            }
+            const int slot = (rb == first_rb) ? 0 : 1;
+            float* part = p.partial + ((int64_t)blockIdx.x * 2 + slot) * kRows * 8;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+            __threadfence();
+            named_sync(1, kConsumers * 32);
+            if (threadIdx.x == 64) {
+                // CTAs covering rb: i_first .. i_last (static schedule).
+                const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
+                const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
+                const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
+                const unsigned prev = atomicAdd(&p.counters[rb], 1u);
+                *s_last = (prev == (unsigned)(ilast - ifirst)) ? 1 : 0;
+                if (*s_last) p.counters[rb] = 0;
+            }
+            named_sync(1, kConsumers * 32);
+            if (*s_last) {
+                __threadfence();
+                const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
+                const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
+                const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int rl = (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
+                    float v = 0.f;
+                    for (int j = ifirst; j <= ilast; ++j) {
+                        const int ju0 = (int)(((int64_t)p.units * j) / gridDim.x);
+                        const int jslot = (ju0 / p.kchunks == rb) ? 0 : 1;
+                        v += __ldcg(p.partial + (((int64_t)j * 2 + jslot) * kRows + rl) * 8 + col);
+                    }
+                    const int row = rb * kRows + rl;
+                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v);
+                }
+            }
+        };
+        for (int i = 0; i < nunits; ++i) {
+            const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
+            if (rb != cur_rb) {
+                if (cur_rb >= 0) flush(cur_rb, rb_first_unit == 0);   // a row block ends inside this CTA
+                cur_rb = rb;
+                if (first_rb < 0) first_rb = rb;
+                rb_first_unit = kc;
+                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            }
+            const int s = i % kStages;
+            const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+            if (!mbar_wait(&xready[s], ph, abort_flag)) break;
+            const uint8_t* cs = s_codes + s * kCodeBytes;
+            const uint8_t* ss = s_scales + s * kScaleBytes;
+            const uint8_t* xf = s_xf + s * kXfBytes;
+            const float* xs = s_xs + s * 8;
+            const float xs0 = xs[2 * c], xs1 = xs[2 * c + 1];
+            if constexpr (FMT == kNVFP4) {
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int su = 0; su < 2; ++su) {
+                    // 16 bytes (32 codes) of rows r0 and r1, 128B-swizzled.
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(cs + r0 * 128 + (((4 * su + c) ^ (r0 & 7)) << 4));
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(cs + r1 * 128 + (((4 * su + c) ^ (r1 & 7)) << 4));
+                    // Scales: 2 groups of 16 codes per row.
+                    const uint32_t sb0 = *reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c);
+                    const uint32_t sb1 = *reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c);
+                    const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)sb0), s1 = e4m3x2_to_f16x2((uint16_t)sb1);
+                    const uint32_t s0lo = __byte_perm(s0, 0, 0x1010), s0hi = __byte_perm(s0, 0, 0x3232);
+                    const uint32_t s1lo = __byte_perm(s1, 0, 0x1010), s1hi = __byte_perm(s1, 0, 0x3232);
+                    const uint32_t wr0[4] = {w0.x, w0.y, w0.z, w0.w};
+                    const uint32_t wr1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int jp = 0; jp < 4; ++jp) {
+                        const uint4 b = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+#pragma unroll
+                        for (int jj = 0; jj < 2; ++jj) {
+                            const int j = 2 * jp + jj;           // step: codes 4j .. 4j + 3 of the chunk
+                            const uint32_t wa = wr0[j >> 1], wb = wr1[j >> 1];
+                            const int byte = (j & 1) * 2;
+                            const uint32_t sa = j < 4 ? s0lo : s0hi, sbb = j < 4 ? s1lo : s1hi;
+                            uint32_t a[4];
+                            a[0] = hmul2u(e2m1_byte(wa, byte), sa);
+                            a[1] = hmul2u(e2m1_byte(wb, byte), sbb);
+                            a[2] = hmul2u(e2m1_byte(wa, byte + 1), sa);
+                            a[3] = hmul2u(e2m1_byte(wb, byte + 1), sbb);
+                            if (jj == 0) mma16816(d, a, b.x, b.y);
+                            else mma16816(d, a, b.z, b.w);
+                        }
+                    }
+                }
+                acc[0] = fmaf(d[0], xs0, acc[0]);
+                acc[1] = fmaf(d[1], xs1, acc[1]);
+                acc[2] = fmaf(d[2], xs0, acc[2]);
+                acc[3] = fmaf(d[3], xs1, acc[3]);
+            } else {
+                // mxfp8: step j covers k [16j, 16j + 16) (one half group);
+                // thread c owns bytes 16j + 4c .. + 3 of each row.
+                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB);
+                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB);
+#pragma unroll
+                for (int grp = 0; grp < 4; ++grp) {
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = 2 * grp + h;
+                        const uint32_t wa = *reinterpret_cast<const uint32_t*>(
+                            cs + r0 * 128 + ((j ^ (r0 & 7)) << 4) + 4 * c);
+                        const uint32_t wb = *reinterpret_cast<const uint32_t*>(
+                            cs + r1 * 128 + ((j ^ (r1 & 7)) << 4) + 4 * c);
+                        uint32_t a[4];
+                        a[0] = e4m3x2_to_f16x2((uint16_t)(wa & 0xFFFF));
+                        a[1] = e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFF));
+                        a[2] = e4m3x2_to_f16x2((uint16_t)(wa >> 16));
+                        a[3] = e4m3x2_to_f16x2((uint16_t)(wb >> 16));
+                        const uint2 b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
+                        mma16816(d, a, b.x, b.y);
+                    }
+                    const float sc0 = ue8m0_to_f32((sw0 >> (8 * grp)) & 0xFF);
+                    const float sc1 = ue8m0_to_f32((sw1 >> (8 * grp)) & 0xFF);
+                    acc[0] = fmaf(d[0], sc0 * xs0, acc[0]);
+                    acc[1] = fmaf(d[1], sc0 * xs1, acc[1]);
+                    acc[2] = fmaf(d[2], sc1 * xs0, acc[2]);
+                    acc[3] = fmaf(d[3], sc1 * xs1, acc[3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (i == nunits - 1) {
+                const bool complete = (kc == p.kchunks - 1) && (rb_first_unit == 0);
+                flush(rb, complete);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ---- per-weight preparation -----------------------------------------------------
+
+__global__ void retile_scales_kernel(const uint8_t* __restrict__ src, int64_t lds, int n, int ngroups,
+                                     int kchunks, int row_blocks, int sb, uint8_t* __restrict__ dst) {
+    // dst[((rb * kchunks + kc) * 128 + r) * sb + b] = src[(rb*128 + r) * lds + kc * sb + b] (0 outside).
+    const int64_t total = (int64_t)row_blocks * kchunks * kRows * sb;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(t % sb);
+        int64_t rest = t / sb;
+        const int r = (int)(rest % kRows);
+        rest /= kRows;
+        const int kc = (int)(rest % kchunks);
+        const int rb = (int)(rest / kchunks);
+        const int row = rb * kRows + r, grp = kc * sb + b;
+        dst[t] = (row < n && grp < ngroups) ? src[(int64_t)row * lds + grp] : (uint8_t)0;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+template <int FMT>
+constexpr int smem_bytes() {
+    return 1024 + kStages * (kCodeBytes + kRows * Cfg<FMT>::SB + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) + 256;
+}
+
+}  // namespace
+
+struct GemvTcState {
+    CUtensorMap cmap;
+    uint8_t* scales_tiled = nullptr;
+    float* partial = nullptr;
+    unsigned int* counters = nullptr;
+    int grid = 0, kchunks = 0, row_blocks = 0;
+};
+
+int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream) {
+    w->tc = nullptr;
+    const int fmt = format_of(w->spec);
+    const int KC = fmt == kMXFP8 ? Cfg<kMXFP8>::KC : Cfg<kNVFP4>::KC;
+    const int SB = fmt == kMXFP8 ? Cfg<kMXFP8>::SB : Cfg<kNVFP4>::SB;
+    if (w->n <= 0 || w->n > INT32_MAX || w->k > INT32_MAX) return QMM_OK;
+    auto enc = encoder();
+    if (!enc) return QMM_OK;
+    DeviceInfo info;
+    if (int rc = device_info(w->device, &info)) return rc;
+    if (info.smem_optin < (size_t)smem_bytes<kNVFP4>()) return QMM_OK;
+    GemvTcState* st = new GemvTcState();
+    st->kchunks = (int)((w->k + KC - 1) / KC);
+    st->row_blocks = (int)((w->n + kRows - 1) / kRows);
+    const int64_t units = (int64_t)st->kchunks * st->row_blocks;
+    if (units > INT32_MAX) { delete st; return QMM_OK; }
+    st->grid = (int)std::min<int64_t>(units, info.sms);
+    const int64_t row_bytes = w->k * w->spec.bits / 8;
+    const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)w->n};
+    const cuuint64_t gstride[1] = {(cuuint64_t)w->ldc};
+    const cuuint32_t box[2] = {128, (cuuint32_t)kRows};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&st->cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->codes, gdim, gstride, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        delete st;
+        return QMM_OK;
+    }
+    const size_t tiled = (size_t)units * kRows * SB;
+    auto fail = [&](cudaError_t e, const char* what) {
+        cudaFree(st->scales_tiled);
+        cudaFree(st->partial);
+        cudaFree(st->counters);
+        delete st;
+        return cuda_error(e, what);
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&st->scales_tiled, tiled)) != cudaSuccess) return fail(e, "cudaMalloc(scales_tiled)");
+    if ((e = cudaMalloc(&st->partial, (size_t)st->grid * 2 * kRows * 8 * sizeof(float))) != cudaSuccess)
+        return fail(e, "cudaMalloc(partial)");
+    if ((e = cudaMalloc(&st->counters, (size_t)st->row_blocks * sizeof(unsigned int))) != cudaSuccess)
+        return fail(e, "cudaMalloc(counters)");
+    if ((e = cudaMemsetAsync(st->counters, 0, (size_t)st->row_blocks * sizeof(unsigned int), stream)) != cudaSuccess)
+        return fail(e, "cudaMemsetAsync(counters)");
+    const int64_t total = (int64_t)tiled;
+    const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)info.sms * 8);
+    retile_scales_kernel<<<grid, 256, 0, stream>>>(w->scales, w->lds, (int)w->n, (int)(w->k / w->spec.group_size),
+                                                   st->kchunks, st->row_blocks, SB, st->scales_tiled);
+    if ((e = cudaGetLastError()) != cudaSuccess) return fail(e, "retile_scales_kernel");
+    w->tc = st;
+    return QMM_OK;
+}
+
+void gemv_tc_release(qmm_weight* w) {
+    if (!w->tc) return;
+    cudaFree(w->tc->scales_tiled);
+    cudaFree(w->tc->partial);
+    cudaFree(w->tc->counters);
+    delete w->tc;
+    w->tc = nullptr;
+}
+
+int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, bool* handled) {
+    *handled = false;
+    const GemvTcState* st = w->tc;
+    if (!st || a.yf || a.m < 1 || a.m > kXRows) return QMM_OK;
+    const auto xa = reinterpret_cast<uintptr_t>(a.x);
+    if ((xa & 15) || ((a.ldx * 2) & 15)) return QMM_OK;
+    const int fmt = a.fmt;
+    const int KC = fmt == kMXFP8 ? Cfg<kMXFP8>::KC : Cfg<kNVFP4>::KC;
+    CUtensorMap xmap;
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)kXRows};
+    const cuuint32_t es[2] = {1, 1};
+    if (encoder()(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return QMM_OK;
+    TcParams p;
+    p.scales_tiled = st->scales_tiled;
+    p.y = a.y;
+    p.partial = st->partial;
+    p.counters = st->counters;
+    p.ldy = a.ldy;
+    p.m = (int)a.m;
+    p.n = (int)a.n;
+    p.k = (int)a.k;
+    p.kchunks = st->kchunks;
+    p.row_blocks = st->row_blocks;
+    p.units = st->kchunks * st->row_blocks;
+    static bool configured[2][64] = {};
+    int dev = w->device;
+    if (fmt == kMXFP8) {
+        if (dev < 64 && !configured[0][dev]) {
+            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kMXFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              smem_bytes<kMXFP8>()));
+            configured[0][dev] = true;
+        }
+        qmm_gemv_tc_kernel<kMXFP8><<<st->grid, kThreads, smem_bytes<kMXFP8>(), stream>>>(st->cmap, xmap, p);
+    } else {
+        if (dev < 64 && !configured[1][dev]) {
+            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kNVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              smem_bytes<kNVFP4>()));
+            configured[1][dev] = true;
+        }
+        qmm_gemv_tc_kernel<kNVFP4><<<st->grid, kThreads, smem_bytes<kNVFP4>(), stream>>>(st->cmap, xmap, p);
+    }
+    QMM_CUDA_TRY(cudaGetLastError());
+    *handled = true;
+    return QMM_OK;
+}
+
+}  // namespace qmm

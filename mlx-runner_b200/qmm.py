@@ -44,7 +44,7 @@ EXPORTS = (
     "qmm_weight_destroy",
     "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
     "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
-    "qmm_last_error", "qmm_error_pending", "qmm_fault_arm", "qmm_fault_fired",
+    "qmm_last_error", "qmm_error_pending", "qmm_device_status", "qmm_fault_arm", "qmm_fault_fired",
 )
 
 
@@ -116,6 +116,7 @@ def lib() -> ctypes.CDLL:
     L.qmm_tp_run_rowparallel.argtypes = [vp, vp, vp, i64, i64, vp, i64, vp]
     L.qmm_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.qmm_fault_arm.argtypes = [ctypes.c_uint64]
+    L.qmm_device_status.argtypes = [vp]
     for name in EXPORTS:
         fn = getattr(L, name)
         if name != "qmm_mode_str":
@@ -136,6 +137,11 @@ def take_error() -> tuple[int, str]:
     buf = ctypes.create_string_buffer(512)
     st = lib().qmm_last_error(buf, len(buf))
     return st, buf.value.decode(errors="replace")
+
+
+def device_status(stream=None) -> None:
+    """Raise QmmError(Timeout) if a kernel gave up a bounded wait."""
+    check(lib().qmm_device_status(_stream_handle(stream)))
 
 
 def fault_arm(k: int) -> None:
