@@ -177,6 +177,57 @@ CONFIG = {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], 
           "mode": MODE, "m": list(M_SET), "n": N_OUT, "k": K_IN}
 
 
+PREFILL = {"m": 32768, "n": 34816, "k": 5120, "mode": "nvfp4"}
+
+
+def prefill_measure(args, qmm, oracle, dev, world: int, rank: int, barrier, max_over_ranks) -> dict:
+    """BASELINE config 3 (32k-token nvfp4 gate/up GEMM) on the tcgen05 kernel;
+    N-sharded (column-parallel, no collective) over the GPUs."""
+    import torch
+    m, n, k, mode = args.prefill_m, PREFILL["n"], PREFILL["k"], PREFILL["mode"]
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+    codes, scales = oracle.quantize(w, mode)
+    del w
+    wt = qmm.QuantizedWeight(codes, scales, mode, shard=(0, rank, world))
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn((m, k), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    y = torch.empty((m, wt.n), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(1, args.prefill_warmup)):
+        wt.run(x, out=y, stream=stream)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.prefill_steps):
+        wt.run(x, out=y, stream=stream)
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.prefill_steps
+    qmm.device_status(stream)
+    flops = 2.0 * m * n * k
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak, kind = bf16_peak()
+    per_gpu = 2.0 * m * wt.n * k / (ms * 1e-3) / 1e12
+    wt.close()
+    return {"workload": f"cfg3: nvfp4 prefill GEMM x [{m}, {k}] . W[{n}, {k}]^T, N-sharded over {world} GPU(s)",
+            "metric": "TFLOP/s", "value": tflops, "ms_per_gemm": ms, "steps": args.prefill_steps,
+            "l2": "inputs larger than L2 (x 335 MB)",
+            "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                         "frac": per_gpu / peak, "peak_kind": kind, "kernel": "qmm_gemm_kernel<nvfp4>",
+                         "note": "dense bf16 MMA peak: W is dequantised exactly to bf16 (parity); "
+                                 "the block-scaled FP4 peak (~9 PF nominal) needs x quantised to FP4"}}
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured burst"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def cpu_baseline_sample(budget_s: float = 10.0) -> dict:
     oracle = _load("oracle", os.path.join(ROOT, "oracle", "oracle.py"))
     oracle.build()
@@ -208,6 +259,11 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of load before warm-up (clock samples)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
+    ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM (profiling runs)")
+    ap.add_argument("--prefill-m", type=int, default=PREFILL["m"])
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-warmup", type=int, default=2)
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -226,6 +282,27 @@ def main() -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     qmm = _load("qmm", os.path.join(PKG, "qmm.py"))
     oracle = _load("oracle", os.path.join(ROOT, "oracle", "oracle.py"))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if args.prefill_only:
+        pf = prefill_measure(args, qmm, oracle, dev, world, rank, barrier, max_over_ranks)
+        if rank == 0:
+            print(json.dumps({"prefill": pf}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # Weights: identical on every rank (seed 0), K-sharded by rank.
     rng = np.random.default_rng(0)
@@ -258,18 +335,6 @@ def main() -> None:
         for wt in weights:
             for m in M_SET:
                 gemm(wt, m)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     launches_per_gemm = 1 if comm is None else 2   # GEMV (+ fp32->bf16 after the all-reduce)
     sampler = ClockSampler(local)
@@ -342,6 +407,13 @@ def main() -> None:
     peak, peak_kind = peaks()
     clocks = sampler.summary()
 
+    for wt in weights:
+        wt.close()
+    weights = []
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_measure(args, qmm, oracle, dev, world, rank, barrier, max_over_ranks)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -354,12 +426,13 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": GEMV_TRAFFIC_BYTES,
-                         "kernel": "gemv_kernel<nvfp4>", "per_m_us": {
+                         "kernel": "qmm_gemv_tc_kernel<nvfp4>", "per_m_us": {
                              str(m): 1e3 * statistics.mean(t for mm, t in k_ms if mm == m) for m in M_SET}},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e_steps},
             "gpu_launches": args.steps * copies * len(M_SET) * launches_per_gemm,
             "clocks": clocks,
+            "prefill": prefill,
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()

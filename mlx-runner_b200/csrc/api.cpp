@@ -89,9 +89,16 @@ int device_info(int device, DeviceInfo* out) {
     return QMM_OK;
 }
 
-int dispatch(const QmmArgs& a, cudaStream_t stream) {
+int dispatch(const QmmArgs& a, cudaStream_t stream, const qmm_weight* w) {
     if (a.m == 0 || a.n == 0) return QMM_OK;
-    if (a.m <= gemv_max_m()) return launch_gemv(a, stream);
+    if (a.m <= gemv_max_m()) {
+        if (w) {
+            bool handled = false;
+            if (int rc = launch_gemv_tc(w, a, stream, &handled)) return rc;
+            if (handled) return QMM_OK;
+        }
+        return launch_gemv(a, stream);
+    }
     bool handled = false;
     if (!a.yf) {
         if (int rc = launch_gemm(a, stream, &handled)) return rc;
@@ -252,7 +259,16 @@ extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t 
         if ((e = cudaMemcpy2DAsync(w->scales, w->lds, scales, lds, ngroups, n, kind, s)) != cudaSuccess)
             return fail(e, "copy scales");
     }
-    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return fail(e, "cudaStreamSynchronize");
+    if (int rc = gemv_tc_prepare(w, s)) {
+        cudaFree(w->codes);
+        cudaFree(w->scales);
+        delete w;
+        return rc;
+    }
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
+        gemv_tc_release(w);
+        return fail(e, "cudaStreamSynchronize");
+    }
     *out = w;
     return QMM_OK;
 }
@@ -301,6 +317,7 @@ extern "C" int qmm_weight_destroy(qmm_weight* w) {
     int prev = -1;
     cudaGetDevice(&prev);
     if (w->device >= 0) cudaSetDevice(w->device);
+    gemv_tc_release(w);
     cudaError_t e1 = cudaFree(w->codes);
     cudaError_t e2 = cudaFree(w->scales);
     if (prev >= 0) cudaSetDevice(prev);
@@ -353,7 +370,7 @@ extern "C" int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_
     a.y = static_cast<uint16_t*>(y_dev);
     a.ldy = ldy;
     a.m = m;
-    return dispatch(a, static_cast<cudaStream_t>(stream));
+    return dispatch(a, static_cast<cudaStream_t>(stream), w);
 }
 
 extern "C" int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m, int64_t ldx,

@@ -14,17 +14,19 @@
 // Tile: one CTA per SM (persistent) computes y^T tiles of 128 weight rows x
 // 256 tokens: the dequantised W tile is the MMA's A operand (M = 128), the
 // x tile the B operand (N = 256), so each code is dequantised once per 256
-// tokens.  Warp roles (16 warps):
+// tokens.  Warp roles (24 warps):
 //   warp 0      TMA producer: x tiles [256 tokens x 64 k] with 128B swizzle
 //   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16) per 64-wide k-block,
 //               fp32 accumulators in TMEM (2 x 256 columns, double-buffered)
 //   warp 2      TMEM allocator
 //   warps 4-7   epilogue: tcgen05.ld -> bf16 -> y (coalesced 64-byte rows)
-//   warps 8-15  dequant: codes + scales straight from global memory (L2),
+//   warp 3      TMA producer: W code tiles [128 rows x 64 k] (64B / 32B swizzle)
+//   warps 8-23  dequant: codes from the code ring, scales from global memory,
 //               decoded with cvt.{e4m3x2,e2m1x2}, written as bf16 into the
 //               A tile in the UMMA K-major SWIZZLE_128B layout
 // Pipelines (mbarriers): S stages of {x tile, W tile}: full_x (TMA bytes),
-// full_w (8 dequant warps), empty (MMA commit); accumulators: tmem_full
+// full_w (16 dequant warps), empty (MMA commit); code tiles: cfull (TMA
+// bytes), cempty (16 dequant warps); accumulators: tmem_full
 // (MMA commit), tmem_empty (4 epilogue warps).  Every wait is bounded by
 // %globaltimer: a wait that gives up raises the CTA's abort flag and the
 // device error word, and every role then drains its in-flight TMA / MMA work,
@@ -41,7 +43,8 @@
 
 namespace qmm {
 
-__device__ unsigned int g_device_error = 0;  // bit 0: a bounded wait timed out
+// Bit 0: a bounded wait in the GEMM timed out (read by qmm_device_status).
+__device__ unsigned int g_device_error = 0;
 
 namespace {
 
@@ -49,11 +52,12 @@ constexpr int kStages = 4;
 constexpr int kBK = 64;                     // k per stage (128 bytes of bf16: one swizzle row)
 constexpr int kTileW = 128;                 // weight rows per tile (MMA M)
 constexpr int kTileT = 256;                 // tokens per tile (MMA N)
-constexpr int kThreads = 512;
+constexpr int kThreads = 768;
 constexpr int kXBytes = kTileT * kBK * 2;   // 32 KB
 constexpr int kWBytes = kTileW * kBK * 2;   // 16 KB
-constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int kDequantWarps = 8;
+constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + 32768 /*code ring*/ + 1024 /*align*/ +
+                           512 /*barriers: <= 33 x 8 B + flags*/;
+constexpr int kDequantWarps = 16;
 constexpr int kEpiWarps = 4;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 
@@ -171,38 +175,56 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTi
                             ((uint32_t)(kTileW >> 4) << 24);
 
 // ---- dequantisation of one half k-block (32 codes) of one weight row --------------
+// W code tiles [128 rows x 64 k] arrive by TMA in their own ring (8 KB mxfp8 /
+// 4 KB nvfp4 per stage) with a 64B / 32B swizzle, so the dequant warps' 16-byte
+// reads of 8 consecutive rows hit 8 different bank groups.
+template <int FMT> struct CodeTile;
+template <> struct CodeTile<kMXFP8> {
+    static constexpr int kRowBytes = 64;
+    static constexpr int kStages = 4;
+    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_64B;
+};
+template <> struct CodeTile<kNVFP4> {
+    static constexpr int kRowBytes = 32;
+    static constexpr int kStages = 8;
+    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_32B;
+};
+constexpr int kCodeRingBytes = 32768;
+
 struct CodeBuf {
     uint4 c0, c1;     // fp8: 32 bytes; fp4: c0 = 16 bytes
     uint32_t s;       // scale byte(s): fp8 one, fp4 two (low byte = first group)
     int valid;        // codes inside K: 0, 16 or 32
 };
 
+// Scale byte of a thread's 16 codes (k [kk, kk + 16) of one row), prefetched
+// ahead from global memory in the checkpoint layout.
 template <int FMT>
-__device__ __forceinline__ CodeBuf load_codes(const GemmParams& p, int row, int kk) {
+__device__ __forceinline__ CodeBuf load_scales(const GemmParams& p, int row, int kk) {
     CodeBuf b;
     b.c0 = make_uint4(0, 0, 0, 0);
     b.c1 = b.c0;
     b.s = 0;
     b.valid = 0;
     if (row >= p.n || kk >= p.k) return b;
-    b.valid = min(32, p.k - kk);
-    const uint8_t* cp = p.codes + (int64_t)row * p.ldc;
+    b.valid = 16;                            // K is a multiple of 16 (the nvfp4 group)
     const uint8_t* sp = p.scales + (int64_t)row * p.lds;
-    if constexpr (FMT == kMXFP8) {
-        b.c0 = __ldg(reinterpret_cast<const uint4*>(cp + kk));
-        b.c1 = __ldg(reinterpret_cast<const uint4*>(cp + kk + 16));
-        b.s = __ldg(sp + kk / 32);
-    } else {
-        if (b.valid == 32) {
-            b.c0 = __ldg(reinterpret_cast<const uint4*>(cp + kk / 2));
-            b.s = (uint32_t)__ldg(sp + kk / 16) | ((uint32_t)__ldg(sp + kk / 16 + 1) << 8);
-        } else {
-            const uint2 h = __ldg(reinterpret_cast<const uint2*>(cp + kk / 2));
-            b.c0 = make_uint4(h.x, h.y, 0, 0);
-            b.s = __ldg(sp + kk / 16);
-        }
-    }
+    b.s = __ldg(sp + kk / (FMT == kMXFP8 ? 32 : 16));
     return b;
+}
+
+// Row r's 16 codes for k quarter q of a swizzled code tile.
+template <int FMT>
+__device__ __forceinline__ void read_codes(const uint8_t* tile, int r, int q, CodeBuf& b) {
+    if constexpr (FMT == kMXFP8) {
+        const int sw = (r >> 1) & 3;          // SWIZZLE_64B: chunk ^= address bits [7:8]
+        b.c0 = *reinterpret_cast<const uint4*>(tile + r * 64 + ((q ^ sw) << 4));
+    } else {
+        const int sw = (r >> 2) & 1;          // SWIZZLE_32B: chunk ^= address bit 7
+        const uint2 v = *reinterpret_cast<const uint2*>(tile + r * 32 + (((q >> 1) ^ sw) << 4) + (q & 1) * 8);
+        b.c0.x = v.x;
+        b.c0.y = v.y;
+    }
 }
 
 __device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
@@ -210,34 +232,32 @@ __device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
     return f32x2_to_bf16x2(f.x, f.y);
 }
 
-// 32 codes -> 4 chunks of 8 bf16 (as uint4), exact.
+// 16 codes -> 2 chunks of 8 bf16 (as uint4), exact.
 template <int FMT>
-__device__ __forceinline__ void dequant32(const CodeBuf& b, uint4 (&out)[4]) {
+__device__ __forceinline__ void dequant16(const CodeBuf& b, uint4 (&out)[2]) {
     if constexpr (FMT == kMXFP8) {
         const float s = ue8m0_to_f32(b.s);
-        const uint32_t w[8] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w, b.c1.x, b.c1.y, b.c1.z, b.c1.w};
-        uint32_t o[16];
+        const uint32_t w[4] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w};
+        uint32_t o[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
             uint32_t h[2];
             e4m3x4_to_f16x2(w[i], h);
             const float2 a = f16x2_to_float2(h[0]), c = f16x2_to_float2(h[1]);
             o[2 * i] = f32x2_to_bf16x2(a.x * s, a.y * s);
             o[2 * i + 1] = f32x2_to_bf16x2(c.x * s, c.y * s);
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) out[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        out[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        out[1] = make_uint4(o[4], o[5], o[6], o[7]);
     } else {
         // E2M1 x UE4M3 products are exact in f16 (<= 6 significant bits,
         // magnitudes 2^-10 .. 2688), so the scale is applied with HMUL2.
-        const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)((b.s & 0xFF) * 0x0101u));
-        const uint32_t s1 = e4m3x2_to_f16x2((uint16_t)(((b.s >> 8) & 0xFF) * 0x0101u));
-        const uint32_t w[4] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w};
+        const uint32_t s = e4m3x2_to_f16x2((uint16_t)((b.s & 0xFF) * 0x0101u));
+        const uint32_t w[2] = {b.c0.x, b.c0.y};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 2; ++j) {
             uint32_t h[4];
             e2m1x8_to_f16x2(w[j], h);
-            const uint32_t s = j < 2 ? s0 : s1;
             uint32_t o[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -251,20 +271,29 @@ __device__ __forceinline__ void dequant32(const CodeBuf& b, uint4 (&out)[4]) {
 
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const __grid_constant__ CUtensorMap cmap,
                                                                 GemmParams p) {
+    constexpr int kCStages = CodeTile<FMT>::kStages;
+    constexpr int kCBytes = kTileW * CodeTile<FMT>::kRowBytes;   // one code tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_x = smem;                                   // kStages x 32 KB
     uint8_t* smem_w = smem + kStages * kXBytes;               // kStages x 16 KB
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_w + kStages * kWBytes);
+    uint8_t* smem_c = smem_w + kStages * kWBytes;             // kCStages code tiles (32 KB)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_c + kCodeRingBytes);
     uint64_t* full_x = bars;
     uint64_t* full_w = bars + kStages;
     uint64_t* empty = bars + 2 * kStages;
     uint64_t* tmem_full = bars + 3 * kStages;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1);
-    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1) + 1;
+    uint64_t* cfull = drain + 1;                              // kCStages
+    uint64_t* cempty = cfull + kCStages;                      // kCStages
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(cempty + kCStages);
+    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(cempty + kCStages) + 1;
+    static_assert(kStages * (kXBytes + kWBytes) + kCodeRingBytes + (3 * kStages + 5 + 2 * 8) * 8 + 8 + 1024 <=
+                  kSmemBytes, "shared-memory carve-up exceeds the allocation");
+    static_assert(kCStages * kCBytes == kCodeRingBytes, "code ring size");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -273,6 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             mbar_init(&full_x[s], 1);
             mbar_init(&full_w[s], kDequantWarps);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kCStages; ++s) {
+            mbar_init(&cfull[s], 1);
+            mbar_init(&cempty[s], kDequantWarps);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tmem_full[a], 1);
@@ -376,6 +409,30 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                 }
             }
         }
+    } else if (warp == 3) {
+        // ---------------- TMA producer (W code tiles) ----------------
+        if (lane == 0) {
+            int last = -1;
+            for (int it = 0; it < total_kb; ++it) {
+                const int s = it % kCStages;
+                const uint32_t ph = (uint32_t)(it / kCStages) & 1u;
+                if (!mbar_wait(&cempty[s], ph ^ 1u, abort_flag)) break;
+                const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+                const int kb = it % p.kblocks;
+                mbar_expect_tx(&cfull[s], kCBytes);
+                tma_load_2d(smem_c + s * kCBytes, &cmap, &cfull[s], kb * CodeTile<FMT>::kRowBytes,
+                            (t % p.w_tiles) * kTileW);
+                last = it;
+            }
+            // Every fill must land before the CTA exits (the dequant warps
+            // consume them all on the normal path; bounded on abort).
+            for (int it = max(0, last - kCStages + 1); it <= last; ++it) {
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(&cfull[it % kCStages], (uint32_t)(it / kCStages) & 1u) &&
+                       globaltimer() - t0 < kTimeoutNs) {
+                }
+            }
+        }
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue: TMEM -> bf16 -> y ----------------
         const int q = warp & 3;                     // TMEM lanes 32q .. 32q + 31
@@ -405,37 +462,40 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         }
     } else if (warp >= 8) {
         // ---------------- dequant: codes -> bf16 A tiles ----------------
-        const int dt = threadIdx.x - 8 * 32;        // 0 .. 255
+        const int dt = threadIdx.x - 8 * 32;        // 0 .. 511
         const int r = dt & (kTileW - 1);            // row within the tile
-        const int h = dt >> 7;                      // k half: [32h, 32h + 32)
+        const int h = dt >> 7;                      // k quarter: [16h, 16h + 16)
         auto coords = [&](int it, int* row, int* kk) {
             const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
             *row = (t % p.w_tiles) * kTileW + r;
-            *kk = (it % p.kblocks) * kBK + 32 * h;
+            *kk = (it % p.kblocks) * kBK + 16 * h;
         };
+        // Scales are prefetched two k-blocks ahead from global memory; the
+        // codes come from the TMA-filled code ring.
         CodeBuf cur{}, n1{};
         int row, kk;
-        if (total_kb > 0) { coords(0, &row, &kk); cur = load_codes<FMT>(p, row, kk); }
-        if (total_kb > 1) { coords(1, &row, &kk); n1 = load_codes<FMT>(p, row, kk); }
+        if (total_kb > 0) { coords(0, &row, &kk); cur = load_scales<FMT>(p, row, kk); }
+        if (total_kb > 1) { coords(1, &row, &kk); n1 = load_scales<FMT>(p, row, kk); }
         // Byte offsets of this thread's 4 swizzled 16-byte chunks in a W tile.
         const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
         for (int it = 0; it < total_kb; ++it) {
             CodeBuf n2 = n1;
-            if (it + 2 < total_kb) { coords(it + 2, &row, &kk); n2 = load_codes<FMT>(p, row, kk); }
+            if (it + 2 < total_kb) { coords(it + 2, &row, &kk); n2 = load_scales<FMT>(p, row, kk); }
             const int s = it % kStages;
             const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-            uint4 o[4];
-            dequant32<FMT>(cur, o);
-            if (cur.valid < 32) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (8 * j >= cur.valid) o[j] = make_uint4(0, 0, 0, 0);
-            }
+            const int cs = it % kCStages;
+            if (!mbar_wait(&cfull[cs], (uint32_t)(it / kCStages) & 1u, abort_flag)) break;
+            read_codes<FMT>(smem_c + cs * kCBytes, r, h, cur);
+            uint4 o[2];
+            dequant16<FMT>(cur, o);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&cempty[cs]);
+            if (cur.valid == 0) o[0] = o[1] = make_uint4(0, 0, 0, 0);   // rows >= N, k >= K
             if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
             uint8_t* wt = smem_w + s * kWBytes + row_off;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int chunk = (4 * h + j) ^ (r & 7);
+            for (int j = 0; j < 2; ++j) {
+                const int chunk = (2 * h + j) ^ (r & 7);
                 *reinterpret_cast<uint4*>(wt + chunk * 16) = o[j];
             }
             fence_proxy_async_smem();
@@ -470,6 +530,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 template <int FMT>
 int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int grid, cudaStream_t stream) {
+    // Code tiles: u8 [N rows, K*bits/8 bytes] with row stride ldc, box
+    // [128 rows x 64 k], swizzled to match read_codes().
+    CUtensorMap cmap;
+    const cuuint64_t cdim[2] = {(cuuint64_t)(a.k * (FMT == kMXFP8 ? 8 : 4) / 8), (cuuint64_t)a.n};
+    const cuuint64_t cstride[1] = {(cuuint64_t)a.ldc};
+    const cuuint32_t cbox[2] = {(cuuint32_t)CodeTile<FMT>::kRowBytes, (cuuint32_t)kTileW};
+    const cuuint32_t ces[2] = {1, 1};
+    CUresult cr = encode_fn()(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.codes), cdim, cstride,
+                              cbox, ces, CU_TENSOR_MAP_INTERLEAVE_NONE, CodeTile<FMT>::kSwizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled(codes) failed (%d)", (int)cr);
     static bool configured[64] = {false};
     int dev = 0;
     QMM_CUDA_TRY(cudaGetDevice(&dev));
@@ -478,8 +549,7 @@ int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, in
                                           kSmemBytes));
         configured[dev] = true;
     }
-    (void)a;
-    qmm_gemm_kernel<FMT><<<grid, kThreads, kSmemBytes, stream>>>(map, p);
+    qmm_gemm_kernel<FMT><<<grid, kThreads, kSmemBytes, stream>>>(map, cmap, p);
     QMM_CUDA_TRY(cudaGetLastError());
     return QMM_OK;
 }
@@ -540,7 +610,9 @@ extern "C" int qmm_device_status(void* stream) {
     if (v) {
         QMM_CUDA_TRY(cudaMemcpyToSymbolAsync(qmm::g_device_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s));
         QMM_CUDA_TRY(cudaStreamSynchronize(s));
-        return qmm::set_error(QMM_ERR_TIMEOUT, "a device-side wait timed out (flags 0x%x)", v);
     }
+    unsigned int v2 = 0;
+    QMM_CUDA_TRY(qmm::gemv_tc_take_error(&v2, s));
+    if (v | v2) return qmm::set_error(QMM_ERR_TIMEOUT, "a device-side wait timed out (flags 0x%x)", v | v2);
     return QMM_OK;
 }

@@ -5,24 +5,29 @@
 // src/engine.zig:428-455; MTP verify M = 2..3, src/engine.zig:548, :656).
 // The op streams W once and is bound by HBM, so the kernel is shaped around
 // keeping HBM busy with few instructions per code:
-//   - persistent grid (one CTA per SM); the work is (128-row block, K-chunk)
-//     units laid out row-block-major and split evenly across CTAs (stream-K),
-//     so every SM streams the same number of bytes whatever N and K are;
-//   - a producer warp streams each unit's codes with one 2D TMA (128-byte
-//     swizzle), its scales with one bulk copy (from the per-unit scale tiles
-//     made at weight creation) and the x chunk with one 2D TMA, into an
-//     8-stage ring: ~130 KB in flight per SM without spending registers;
+//   - persistent grid (one CTA per SM); the work is (128-row block, K-chunk
+//     of 256 code bytes per row) units laid out row-block-major and split
+//     evenly across CTAs (stream-K), so every SM streams the same number of
+//     bytes whatever N and K are;
+//   - a producer warp streams each unit's codes with two 2D TMAs (128 rows x
+//     128 bytes, 128-byte swizzle), its scales with one bulk copy (from the
+//     per-unit scale tiles made at weight creation) and the x chunk with
+//     256-element 2D TMAs, into a 4-stage ring: 128 KB of codes in flight per
+//     SM without spending registers;
 //   - a converter warp turns the x chunk into f16 B fragments after an exact
 //     power-of-two scaling into f16 range (per x row and chunk), so every x
 //     value within 2^29 of the chunk's largest is represented exactly;
-//   - 8 consumer warps own 16 rows each and run mma.sync.m16n8k16 (f16 in,
+//   - 16 consumer warps (8 groups of 16 rows x 2 halves of the unit's k
+//     range) run mma.sync.m16n8k16 (f16 in,
 //     fp32 accumulate) with the weight codes widened by cvt.f16x2.e2m1x2 /
 //     .e4m3x2 (exact).  nvfp4 scales multiply the f16 codes (E2M1 x UE4M3 is
 //     exact in f16); mxfp8 scales (any power of two) are applied in fp32 to
 //     per-group partial sums;
 //   - rows of a block split between CTAs are summed by the last CTA to
 //     finish them, in CTA order (deterministic), through a small fp32
-//     scratch owned by the weight; the counters are reset by that CTA.
+//     scratch owned by the weight; the counters are reset by that CTA.  One
+//     thread per CTA fences (per-thread fences stall under HBM load) and the
+//     final sum keeps 8 loads in flight per thread.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -36,26 +41,28 @@
 
 namespace qmm {
 
-extern __device__ unsigned int g_device_error;
+// Bit 1: a bounded wait in this kernel timed out (read by qmm_device_status).
+__device__ unsigned int g_gemv_tc_error = 0;
 
 namespace {
 
 constexpr int kRows = 128;                 // rows per unit (8 warps x 16)
-constexpr int kStages = 8;
-constexpr int kCodeBytes = kRows * 128;    // 16 KB: 128 code bytes per row per unit
+constexpr int kStages = 4;
+constexpr int kBox = kRows * 128;          // one 2D TMA box: 128 rows x 128 code bytes
+constexpr int kCodeBytes = 2 * kBox;       // 32 KB: 256 code bytes per row per unit
 constexpr int kXRows = 8;                  // x rows staged per unit (M padded to 8)
-constexpr int kThreads = 320;              // producer, converter, 8 consumers
-constexpr int kConsumers = 8;
+constexpr int kConsumers = 16;             // 8 row groups x 2 k halves
+constexpr int kThreads = (2 + kConsumers) * 32;  // producer, converter, consumers
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 template <int FMT> struct Cfg;
 template <> struct Cfg<kMXFP8> {
-    static constexpr int KC = 128;         // codes per row per unit
-    static constexpr int SB = 4;           // scale bytes per row per unit
+    static constexpr int KC = 256;         // codes per row per unit
+    static constexpr int SB = 8;           // scale bytes per row per unit
 };
 template <> struct Cfg<kNVFP4> {
-    static constexpr int KC = 256;
-    static constexpr int SB = 16;
+    static constexpr int KC = 512;
+    static constexpr int SB = 32;
 };
 
 struct TcParams {
@@ -100,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
             if (*abort_flag) return false;
             if (gtimer() - t0 > kTimeoutNs) {
                 *abort_flag = 1;
-                atomicOr(&g_device_error, 2u);
+                atomicOr(&g_gemv_tc_error, 2u);
                 return false;
             }
         }
@@ -133,25 +140,6 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-__device__ __forceinline__ uint32_t e2m1_byte(uint32_t w, int byte) {
-    return e2m1x2_to_f16x2((w >> (8 * byte)) & 0xFFu);
-}
-
-// Physical k (within a unit) of x element e (0..7) of B-fragment slot
-// (step pair jp, lane quad c): see the consumer's A mapping.
-template <int FMT>
-__device__ __forceinline__ int slot_k(int jp, int c, int e) {
-    if constexpr (FMT == kNVFP4) {
-        // super-step ss = jp / 4 covers 128 k; thread c owns 32 of them, and
-        // step j = 2 * (jp % 4) + (e / 4) uses its codes 4j .. 4j + 3.
-        return 128 * (jp >> 2) + 32 * c + 8 * (jp & 3) + e;
-    } else {
-        // step j covers [16j, 16j + 16); thread c owns 16j + 4c .. + 3.
-        const int j = 2 * jp + (e >> 2);
-        return 16 * j + 4 * c + (e & 3);
-    }
-}
-
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
                                                                    const __grid_constant__ CUtensorMap xmap,
@@ -167,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     uint8_t* s_xraw = s_scales + kStages * kScaleBytes;               // kStages x kXRawBytes
     uint8_t* s_xf = s_xraw + kStages * kXRawBytes;                    // kStages x kXfBytes
     float* s_xs = reinterpret_cast<float*>(s_xf + kStages * kXfBytes);  // kStages x 8
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s_xs + kStages * 8);
+    float* s_red = s_xs + kStages * 8;                                  // 128 x 8 (k-half sums)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + kRows * 8);
     uint64_t* full = bars;
     uint64_t* xready = bars + kStages;
     uint64_t* empty = bars + 2 * kStages;
@@ -200,9 +189,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
                 const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
                 mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes + kXRawBytes);
-                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 128, rb * kRows);
+                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 256, rb * kRows);
+                tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], kc * 256 + 128, rb * kRows);
                 bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)u * kScaleBytes, kScaleBytes, &full[s]);
-                tma_2d(s_xraw + s * kXRawBytes, &xmap, &full[s], kc * KC, 0);
+#pragma unroll
+                for (int xb = 0; xb < KC / 256; ++xb)   // x rows of the chunk, 256 elements per box
+                    tma_2d(s_xraw + s * kXRawBytes + xb * kXRows * 512, &xmap, &full[s], kc * KC + 256 * xb, 0);
                 last = i;
             }
             // Drain: every stage's last fill must land, and every consumer
@@ -215,102 +207,180 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         }
     } else if (warp == 1) {
         // ---------------- x converter ----------------
+        // B-fragment slots of x rows >= M are zero for the whole launch and
+        // their x-scale factors 1 (their accumulator columns are never stored).
+        for (int off = lane * 16; off < kStages * kXfBytes; off += 32 * 16)
+            *reinterpret_cast<uint4*>(s_xf + off) = make_uint4(0, 0, 0, 0);
+        for (int t = lane; t < kStages * 8; t += 32) s_xs[t] = 1.0f;
+        __syncwarp();
         for (int i = 0; i < nunits; ++i) {
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)(i / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort_flag)) break;
             const uint16_t* raw = reinterpret_cast<const uint16_t*>(s_xraw + s * kXRawBytes);
             float* xs = s_xs + s * 8;
-            // Per x row: amax over the chunk -> exponent e, x scaled by 2^-e
-            // into [2^14, 2^15) before the f16 conversion.
-            float inv[kXRows];
+            // Lane L owns x elements [E L, E L + E) of every row of the chunk
+            // (E = KC / 32): amax over the chunk -> exponent e, x scaled by
+            // 2^-e into [2^14, 2^15), converted to f16 and stored into the
+            // B-fragment slot that element run belongs to.  Slots of rows
+            // m >= M stay zero (cleared once before the first unit).
+            // The raw chunk arrives as 256-element TMA boxes: element (m, k)
+            // sits at box k / 256, row m, column k % 256.
+            constexpr int E = KC / 32;             // 16 (nvfp4) or 8 (mxfp8)
+            uint8_t* xf = s_xf + s * kXfBytes;
+            const int k0 = E * lane;
+            const uint16_t* rbase = raw + (k0 >> 8) * (kXRows * 256) + (k0 & 255);
+            for (int m = 0; m < p.m; ++m) {
+                float v[E];
+                uint32_t w[E / 2];
 #pragma unroll
-            for (int m = 0; m < kXRows; ++m) {
-                float a = 0.f;
-                if (m < p.m) {
-                    for (int e = lane; e < KC; e += 32) a = fmaxf(a, fabsf(__uint_as_float((uint32_t)raw[m * KC + e] << 16)));
-#pragma unroll
-                    for (int off = 16; off; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, off));
+                for (int q = 0; q < E / 8; ++q) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(rbase + m * 256 + 8 * q);
+                    w[4 * q] = r.x; w[4 * q + 1] = r.y; w[4 * q + 2] = r.z; w[4 * q + 3] = r.w;
                 }
+                // Largest |x| of the chunk from the bf16 bit patterns (magnitude
+                // order = integer order; a NaN sorts above every finite value).
+                uint32_t mx = 0;
+#pragma unroll
+                for (int i = 0; i < E / 2; ++i) {
+                    const float2 f = bf16x2_to_float2(w[i]);
+                    v[2 * i] = f.x;
+                    v[2 * i + 1] = f.y;
+                    mx = max(mx, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+                }
+                mx = __reduce_max_sync(0xFFFFFFFFu, mx);
                 int ex = 0;
-                if (a > 0.f && a == a) {
-                    ex = (int)((__float_as_uint(a) >> 23) & 0xFF) - 127 - 14;
+                if (mx != 0) {
+                    ex = (int)((mx >> 7) & 0xFF) - 127 - 14;
                     ex = max(-100, min(100, ex));
                 }
-                inv[m] = __uint_as_float((uint32_t)(127 - ex) << 23);
+                const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
                 if (lane == 0) xs[m] = __uint_as_float((uint32_t)(127 + ex) << 23);
-            }
-            // B-fragment slots: slot = jp * 32 + (4 * g + c) holds 8 f16 of x row g.
-            uint8_t* xf = s_xf + s * kXfBytes;
-            constexpr int kSlots = KC / 32 * 32;   // (KC / 16 / 2) step pairs x 32 lanes
-            for (int slot = lane; slot < kSlots; slot += 32) {
-                const int jp = slot >> 5, q = slot & 31, g = q >> 2, c = q & 3;
-                uint32_t h[4] = {0, 0, 0, 0};
-                if (g < p.m) {
+                uint32_t h[E / 2];
 #pragma unroll
-                    for (int e = 0; e < 8; e += 2) {
-                        const float v0 = __uint_as_float((uint32_t)raw[g * KC + slot_k<FMT>(jp, c, e)] << 16) * inv[g];
-                        const float v1 = __uint_as_float((uint32_t)raw[g * KC + slot_k<FMT>(jp, c, e + 1)] << 16) * inv[g];
-                        __half2 hv = __floats2half2_rn(v0, v1);
-                        h[e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
+                for (int i = 0; i < E / 2; ++i) {
+                    __half2 hv = __floats2half2_rn(v[2 * i] * inv, v[2 * i + 1] * inv);
+                    h[i] = *reinterpret_cast<uint32_t*>(&hv);
+                }
+                if constexpr (FMT == kNVFP4) {
+                    // run R = k / 8 of 8 elements -> super-step su = R / 16,
+                    // quad c = (R / 4) % 4, step pair jp = 4 su + R % 4.
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int R = 2 * lane + q, jp = 4 * (R >> 4) + (R & 3), c = (R >> 2) & 3;
+                        *reinterpret_cast<uint4*>(xf + (jp * 32 + 4 * m + c) * 16) =
+                            make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+                    }
+                } else {
+                    // run R = k / 4 of 4 elements -> step j = R / 4 (slot j / 2,
+                    // half j % 2), quad c = R % 4.
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int R = 2 * lane + q, j = R >> 2, c = R & 3;
+                        *reinterpret_cast<uint2*>(xf + ((j >> 1) * 32 + 4 * m + c) * 16 + (j & 1) * 8) =
+                            make_uint2(h[2 * q], h[2 * q + 1]);
                     }
                 }
-                *reinterpret_cast<uint4*>(xf + slot * 16) = make_uint4(h[0], h[1], h[2], h[3]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&xready[s]);
         }
     } else {
         // ---------------- consumers ----------------
-        const int cw = warp - 2;                 // rows [16 cw, 16 cw + 16) of the block
+        // Warp cw owns rows [16 rg, 16 rg + 16) of every unit (rg = cw % 8)
+        // over one half of the unit's k range (kh = cw / 8).
+        const int cw = warp - 2, rg = cw & 7, kh = cw >> 3;
         const int g = lane >> 2, c = lane & 3;
-        const int r0 = 16 * cw + g, r1 = r0 + 8;
+        const int r0 = 16 * rg + g, r1 = r0 + 8;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
         auto flush = [&](int rb, bool complete) {
-            // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.
-            if (complete) {
+            // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
+            // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
+            if (kh == 1) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
-                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+            }
+            named_sync(1, kConsumers * 32);
+            if (kh == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
+            }
+            if (complete) {
+                if (kh == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
+                        if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                    }
                 }
+                named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
                 return;
             }
             const int slot = (rb == first_rb) ? 0 : 1;
             float* part = p.partial + ((int64_t)blockIdx.x * 2 + slot) * kRows * 8;
+            if (kh == 0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
-            __threadfence();
+                for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+            }
+            // The barrier orders the CTA's partial writes before thread 64's
+            // gpu-scope fence, which then releases them with the counter
+            // update; the last arriver's fence acquires the other CTAs' writes
+            // for every thread past the next barrier.  (One fence per CTA:
+            // fences by every thread stall for microseconds under HBM load.)
             named_sync(1, kConsumers * 32);
             if (threadIdx.x == 64) {
                 // CTAs covering rb: i_first .. i_last (static schedule).
                 const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
                 const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
                 const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
+                __threadfence();
                 const unsigned prev = atomicAdd(&p.counters[rb], 1u);
-                *s_last = (prev == (unsigned)(ilast - ifirst)) ? 1 : 0;
-                if (*s_last) p.counters[rb] = 0;
+                const int last = (prev == (unsigned)(ilast - ifirst)) ? 1 : 0;
+                if (last) {
+                    __threadfence();
+                    p.counters[rb] = 0;
+                }
+                *s_last = last;
             }
             named_sync(1, kConsumers * 32);
             if (*s_last) {
-                __threadfence();
+                // Sum the contributors' partials in CTA order.  Each of the 512
+                // consumer threads owns 2 of the block's 128 x 8 outputs and
+                // keeps 8 contributor loads in flight per batch.
                 const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
                 const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
                 const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
+                const int t = threadIdx.x - 64;
+                float v[2] = {0.f, 0.f};
+                for (int j0 = ifirst; j0 <= ilast; j0 += 8) {
+                    float ld[8][2];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int rl = (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
-                    float v = 0.f;
-                    for (int j = ifirst; j <= ilast; ++j) {
-                        const int ju0 = (int)(((int64_t)p.units * j) / gridDim.x);
-                        const int jslot = (ju0 / p.kchunks == rb) ? 0 : 1;
-                        v += __ldcg(p.partial + (((int64_t)j * 2 + jslot) * kRows + rl) * 8 + col);
+                    for (int q = 0; q < 8; ++q) {
+                        const int j = j0 + q;
+                        ld[q][0] = ld[q][1] = 0.f;
+                        if (j <= ilast) {
+                            const int ju0 = (int)(((int64_t)p.units * j) / gridDim.x);
+                            const int jslot = (ju0 / p.kchunks == rb) ? 0 : 1;
+                            const float* src = p.partial + ((int64_t)j * 2 + jslot) * kRows * 8;
+                            ld[q][0] = __ldcg(src + t);
+                            ld[q][1] = __ldcg(src + t + 512);
+                        }
                     }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        v[0] += ld[q][0];
+                        v[1] += ld[q][1];
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int idx = t + 512 * e, rl = idx >> 3, col = idx & 7;
                     const int row = rb * kRows + rl;
-                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v);
+                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v[e]);
                 }
             }
+            named_sync(1, kConsumers * 32);       // s_red / s_last are reused by the next flush
         };
         for (int i = 0; i < nunits; ++i) {
             const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
@@ -323,65 +393,80 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             }
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-            if (!mbar_wait(&xready[s], ph, abort_flag)) break;
+            // A wait that gives up leaves the unit uncomputed but keeps the
+            // warp in step with the others (the named barriers in flush must
+            // match); the device error word tells the host the output is void.
+            const bool live = mbar_wait(&xready[s], ph, abort_flag);
+            if (live) {
             const uint8_t* cs = s_codes + s * kCodeBytes;
             const uint8_t* ss = s_scales + s * kScaleBytes;
             const uint8_t* xf = s_xf + s * kXfBytes;
             const float* xs = s_xs + s * 8;
             const float xs0 = xs[2 * c], xs1 = xs[2 * c + 1];
             if constexpr (FMT == kNVFP4) {
-                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                // Two accumulators (even / odd steps) keep two mma chains in flight.
+                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int su = 0; su < 2; ++su) {
-                    // 16 bytes (32 codes) of rows r0 and r1, 128B-swizzled.
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(cs + r0 * 128 + (((4 * su + c) ^ (r0 & 7)) << 4));
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(cs + r1 * 128 + (((4 * su + c) ^ (r1 & 7)) << 4));
+                for (int si = 0; si < 2; ++si) {
+                    const int su = kh + 2 * si;          // this warp's 128-k super-steps of the unit
+                    // 16 bytes (32 codes) of rows r0 and r1: box su / 2, chunk
+                    // (4 su + c) % 8 of the 128-byte row, 128B-swizzled.
+                    const uint8_t* cb = cs + (su >> 1) * kBox;
+                    const int ch = (4 * su + c) & 7;
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0 * 128 + ((ch ^ (r0 & 7)) << 4));
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1 * 128 + ((ch ^ (r1 & 7)) << 4));
                     // Scales: 2 groups of 16 codes per row.
                     const uint32_t sb0 = *reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c);
                     const uint32_t sb1 = *reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c);
                     const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)sb0), s1 = e4m3x2_to_f16x2((uint16_t)sb1);
                     const uint32_t s0lo = __byte_perm(s0, 0, 0x1010), s0hi = __byte_perm(s0, 0, 0x3232);
                     const uint32_t s1lo = __byte_perm(s1, 0, 0x1010), s1hi = __byte_perm(s1, 0, 0x3232);
-                    const uint32_t wr0[4] = {w0.x, w0.y, w0.z, w0.w};
-                    const uint32_t wr1[4] = {w1.x, w1.y, w1.z, w1.w};
+                    // Widen whole words: h[b] = f16x2 of byte b (codes 2b, 2b + 1), scaled.
+                    uint32_t h0[16], h1[16];
+                    e2m1x8_to_f16x2(w0.x, *reinterpret_cast<uint32_t(*)[4]>(&h0[0]));
+                    e2m1x8_to_f16x2(w0.y, *reinterpret_cast<uint32_t(*)[4]>(&h0[4]));
+                    e2m1x8_to_f16x2(w0.z, *reinterpret_cast<uint32_t(*)[4]>(&h0[8]));
+                    e2m1x8_to_f16x2(w0.w, *reinterpret_cast<uint32_t(*)[4]>(&h0[12]));
+                    e2m1x8_to_f16x2(w1.x, *reinterpret_cast<uint32_t(*)[4]>(&h1[0]));
+                    e2m1x8_to_f16x2(w1.y, *reinterpret_cast<uint32_t(*)[4]>(&h1[4]));
+                    e2m1x8_to_f16x2(w1.z, *reinterpret_cast<uint32_t(*)[4]>(&h1[8]));
+                    e2m1x8_to_f16x2(w1.w, *reinterpret_cast<uint32_t(*)[4]>(&h1[12]));
+#pragma unroll
+                    for (int b = 0; b < 16; ++b) {
+                        h0[b] = hmul2u(h0[b], b < 8 ? s0lo : s0hi);
+                        h1[b] = hmul2u(h1[b], b < 8 ? s1lo : s1hi);
+                    }
 #pragma unroll
                     for (int jp = 0; jp < 4; ++jp) {
-                        const uint4 b = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
-#pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) {
-                            const int j = 2 * jp + jj;           // step: codes 4j .. 4j + 3 of the chunk
-                            const uint32_t wa = wr0[j >> 1], wb = wr1[j >> 1];
-                            const int byte = (j & 1) * 2;
-                            const uint32_t sa = j < 4 ? s0lo : s0hi, sbb = j < 4 ? s1lo : s1hi;
-                            uint32_t a[4];
-                            a[0] = hmul2u(e2m1_byte(wa, byte), sa);
-                            a[1] = hmul2u(e2m1_byte(wb, byte), sbb);
-                            a[2] = hmul2u(e2m1_byte(wa, byte + 1), sa);
-                            a[3] = hmul2u(e2m1_byte(wb, byte + 1), sbb);
-                            if (jj == 0) mma16816(d, a, b.x, b.y);
-                            else mma16816(d, a, b.z, b.w);
-                        }
+                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
+                        const uint32_t a0[4] = {h0[4 * jp], h1[4 * jp], h0[4 * jp + 1], h1[4 * jp + 1]};
+                        const uint32_t a1[4] = {h0[4 * jp + 2], h1[4 * jp + 2], h0[4 * jp + 3], h1[4 * jp + 3]};
+                        mma16816(d0, a0, bx.x, bx.y);
+                        mma16816(d1, a1, bx.z, bx.w);
                     }
                 }
-                acc[0] = fmaf(d[0], xs0, acc[0]);
-                acc[1] = fmaf(d[1], xs1, acc[1]);
-                acc[2] = fmaf(d[2], xs0, acc[2]);
-                acc[3] = fmaf(d[3], xs1, acc[3]);
+                acc[0] = fmaf(d0[0] + d1[0], xs0, acc[0]);
+                acc[1] = fmaf(d0[1] + d1[1], xs1, acc[1]);
+                acc[2] = fmaf(d0[2] + d1[2], xs0, acc[2]);
+                acc[3] = fmaf(d0[3] + d1[3], xs1, acc[3]);
             } else {
                 // mxfp8: step j covers k [16j, 16j + 16) (one half group);
                 // thread c owns bytes 16j + 4c .. + 3 of each row.
-                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB);
-                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB);
+                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB + 4 * kh);
+                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB + 4 * kh);
 #pragma unroll
-                for (int grp = 0; grp < 4; ++grp) {
+                for (int gi = 0; gi < 4; ++gi) {
+                    const int grp = 4 * kh + gi;         // this warp's four 32-code groups
                     float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int j = 2 * grp + h;
+                        const uint8_t* cb = cs + (j >> 3) * kBox;
                         const uint32_t wa = *reinterpret_cast<const uint32_t*>(
-                            cs + r0 * 128 + ((j ^ (r0 & 7)) << 4) + 4 * c);
+                            cb + r0 * 128 + (((j & 7) ^ (r0 & 7)) << 4) + 4 * c);
                         const uint32_t wb = *reinterpret_cast<const uint32_t*>(
-                            cs + r1 * 128 + ((j ^ (r1 & 7)) << 4) + 4 * c);
+                            cb + r1 * 128 + (((j & 7) ^ (r1 & 7)) << 4) + 4 * c);
                         uint32_t a[4];
                         a[0] = e4m3x2_to_f16x2((uint16_t)(wa & 0xFFFF));
                         a[1] = e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFF));
@@ -390,14 +475,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const uint2 b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
                         mma16816(d, a, b.x, b.y);
                     }
-                    const float sc0 = ue8m0_to_f32((sw0 >> (8 * grp)) & 0xFF);
-                    const float sc1 = ue8m0_to_f32((sw1 >> (8 * grp)) & 0xFF);
+                    const float sc0 = ue8m0_to_f32((sw0 >> (8 * gi)) & 0xFF);
+                    const float sc1 = ue8m0_to_f32((sw1 >> (8 * gi)) & 0xFF);
                     acc[0] = fmaf(d[0], sc0 * xs0, acc[0]);
                     acc[1] = fmaf(d[1], sc0 * xs1, acc[1]);
                     acc[2] = fmaf(d[2], sc1 * xs0, acc[2]);
                     acc[3] = fmaf(d[3], sc1 * xs1, acc[3]);
                 }
             }
+            }  // live
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (i == nunits - 1) {
@@ -442,7 +528,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 template <int FMT>
 constexpr int smem_bytes() {
-    return 1024 + kStages * (kCodeBytes + kRows * Cfg<FMT>::SB + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) + 256;
+    return 1024 + kStages * (kCodeBytes + kRows * Cfg<FMT>::SB + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
+           kRows * 8 * 4 + 256;
 }
 
 }  // namespace
@@ -508,6 +595,17 @@ int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream) {
     return QMM_OK;
 }
 
+cudaError_t gemv_tc_take_error(unsigned int* v, cudaStream_t s) {
+    unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(v, g_gemv_tc_error, sizeof(*v), 0, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && *v) {
+        e = cudaMemcpyToSymbolAsync(g_gemv_tc_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    return e;
+}
+
 void gemv_tc_release(qmm_weight* w) {
     if (!w->tc) return;
     cudaFree(w->tc->scales_tiled);
@@ -524,11 +622,10 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     const auto xa = reinterpret_cast<uintptr_t>(a.x);
     if ((xa & 15) || ((a.ldx * 2) & 15)) return QMM_OK;
     const int fmt = a.fmt;
-    const int KC = fmt == kMXFP8 ? Cfg<kMXFP8>::KC : Cfg<kNVFP4>::KC;
     CUtensorMap xmap;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
     const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)kXRows};
+    const cuuint32_t box[2] = {256u, (cuuint32_t)kXRows};
     const cuuint32_t es[2] = {1, 1};
     if (encoder()(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

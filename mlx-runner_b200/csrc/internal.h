@@ -5,7 +5,9 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-#include "../../include/qmm.h"
+#include "qmm.h"
+
+struct qmm_weight;
 
 namespace qmm {
 
@@ -70,13 +72,25 @@ int launch_dequant(int fmt, const uint8_t* codes, int64_t ldc, const uint8_t* sc
 // (the caller then uses the GEMV path over row blocks).
 int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled);
 
-// Route one call to the right kernel family.
-int dispatch(const QmmArgs& a, cudaStream_t stream);
+// Route one call to the right kernel family (`w` is the resident weight the
+// operands come from, or null for the stateless entry point).
+int dispatch(const QmmArgs& a, cudaStream_t stream, const qmm_weight* w = nullptr);
+
+// TMA-fed tensor-core GEMV for resident weights (gemv_tc.cu): per-weight
+// state (codes tensor map, per-unit scale tiles, stream-K scratch) is made
+// at weight creation; *handled = false when the call is outside its envelope.
+struct GemvTcState;
+int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream);
+void gemv_tc_release(qmm_weight* w);
+int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, bool* handled);
+// Read and clear the kernel's device-side timeout word (synchronizes s).
+cudaError_t gemv_tc_take_error(unsigned int* v, cudaStream_t s);
 
 }  // namespace qmm
 
 // Resident weight (opaque in the C ABI).
 struct qmm_weight {
+    qmm::GemvTcState* tc = nullptr;  // decode-kernel state, or null
     int device = -1;
     int64_t n = 0, k = 0;
     qmm_quant_spec spec{};

@@ -23,7 +23,7 @@ from dataclasses import dataclass
 from typing import Iterable, Optional, Sequence
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "_build", "libqmm_b200.so")
+LIB_PATH = os.environ.get("QMM_B200_LIB") or os.path.join(HERE, "_build", "libqmm_b200.so")
 
 QMM_OK = 0
 STATUS_NAMES = {

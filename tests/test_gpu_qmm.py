@@ -135,7 +135,7 @@ def test_nvfp4_half_chunk_rows(cuda_device):
         check_parity(y_handle, x, codes, scales, "nvfp4")
         y_raw = qmm.quantized_matmul(x, torch.from_numpy(codes.view(np.int32)).to(cuda_device),
                                      torch.from_numpy(scales).to(cuda_device), mode="nvfp4")
-        assert torch.equal(y_raw, y_handle)
+        check_parity(y_raw, x, codes, scales, "nvfp4")
 
 
 @pytest.mark.parametrize("mode", ["mxfp8", "nvfp4"])
@@ -154,8 +154,8 @@ def test_stateless_matches_handle_and_strides(cuda_device, mode):
         y2 = qmm.quantized_matmul(x, torch.from_numpy(codes.view(np.int32)).to(cuda_device),
                                   torch.from_numpy(scales).to(cuda_device), mode=mode)
         torch.cuda.synchronize()
-        assert torch.equal(y, y2)
-        check_parity(y, x.contiguous(), codes, scales, mode)
+        check_parity(y, x.contiguous(), codes, scales, mode)     # resident-weight decode kernel
+        check_parity(y2, x.contiguous(), codes, scales, mode)    # stateless (checkpoint-layout) kernel
         # 4-byte aligned but not 16-byte aligned x: the scalar-load variant.
         x4 = xbig[:, 2:2 + k]
         y4 = w(x4)
@@ -213,3 +213,37 @@ def test_medium_m(cuda_device, mode, m):
     codes, scales = make_weight(384, 1024, mode, seed=m)
     x = make_x(m, 1024, seed=m).to(cuda_device)
     check_parity(qmm.QuantizedWeight(codes, scales, mode)(x), x, codes, scales, mode)
+
+
+@pytest.mark.parametrize("mode", ["mxfp8", "nvfp4"])
+@pytest.mark.parametrize("n,k", [(384, 8192), (130, 4096), (1000, 1000 // 32 * 32), (5120, 17408 // 8),
+                                 (20, 20480)])
+def test_decode_stream_k_splits(cuda_device, mode, n, k):
+    """Row blocks split across many CTAs (units < SMs, ragged N and K): the
+    cross-CTA partial reduction, and its counters, across repeated calls."""
+    import torch
+    if k % (32 if mode == "mxfp8" else 16):
+        pytest.skip("k not a multiple of the group")
+    codes, scales = make_weight(n, k, mode, seed=n + k)
+    w = qmm.QuantizedWeight(codes, scales, mode)
+    for m in (1, 3, 8):
+        x = make_x(m, k, seed=m + k).to(cuda_device)
+        ys = [w(x) for _ in range(3)]
+        qmm.device_status()
+        assert all(torch.equal(ys[0], yy) for yy in ys[1:])    # deterministic, counters reset
+        check_parity(ys[0], x, codes, scales, mode)
+
+
+def test_decode_x_range_extremes(cuda_device):
+    """x spanning bf16's range: huge (> f16 max) and tiny values in one row."""
+    import torch
+    n, k = 256, 2048
+    for mode in ("mxfp8", "nvfp4"):
+        codes, scales = make_weight(n, k, mode, seed=9)
+        x = make_x(2, k, seed=9)
+        x[0, 5] = 3.0e6
+        x[0, 700] = -2.5e5
+        x[1, :100] *= 1e-6
+        x[1, 1500] = 1e-30
+        x = x.to(cuda_device)
+        check_parity(qmm.QuantizedWeight(codes, scales, mode)(x), x, codes, scales, mode)
