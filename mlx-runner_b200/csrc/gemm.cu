@@ -11,24 +11,28 @@
 // (Quantising x to FP8/FP4 for the block-scaled MMA kinds would add
 // 2-10% error per element, far outside the 2e-3 tolerance.)
 //
-// Tile: one CTA per SM (persistent) computes y^T tiles of 128 weight rows x
-// 256 tokens: the dequantised W tile is the MMA's A operand (M = 128), the
-// x tile the B operand (N = 256), so each code is dequantised once per 256
-// tokens.  Warp roles (24 warps):
-//   warp 0      TMA producer: x tiles [256 tokens x 64 k] with 128B swizzle
-//   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16) per 64-wide k-block,
-//               fp32 accumulators in TMEM (2 x 256 columns, double-buffered)
-//   warp 2      TMEM allocator
+// The expensive step is the dequantisation (the fp8/fp4 -> f16 conversions
+// run at a quarter of the fp32 rate on sm_100), so the tile is shaped to
+// dequantise each code once per 512 tokens: one CTA per SM (persistent)
+// computes y^T tiles of 128 weight rows x 512 tokens.  Per 32-wide k-block
+// the dequantised W tile is the A operand (M = 128) of two MMAs whose B
+// operands are the two 256-token halves of the x tile, accumulating into the
+// two 256-column halves of TMEM.  Warp roles (24 warps):
+//   warp 0      TMA producer: x tiles [2 x 256 tokens x 32 k], 64B swizzle
+//   warp 1      MMA issuer: 2 k16 steps x 2 halves of tcgen05.mma kind::f16
+//   warp 2      TMEM allocator (512 columns: one 128 x 512 fp32 tile)
+//   warp 3      TMA producer: W code tiles [128 rows x 32 k]
 //   warps 4-7   epilogue: tcgen05.ld -> bf16 -> y (coalesced 64-byte rows)
-//   warp 3      TMA producer: W code tiles [128 rows x 64 k] (64B / 32B swizzle)
-//   warps 8-23  dequant: codes from the code ring, scales from global memory,
-//               decoded with cvt.{e4m3x2,e2m1x2}, written as bf16 into the
-//               A tile in the UMMA K-major SWIZZLE_128B layout
-// Pipelines (mbarriers): S stages of {x tile, W tile}: full_x (TMA bytes),
-// full_w (16 dequant warps), empty (MMA commit); code tiles: cfull (TMA
-// bytes), cempty (16 dequant warps); accumulators: tmem_full
-// (MMA commit), tmem_empty (4 epilogue warps).  Every wait is bounded by
-// %globaltimer: a wait that gives up raises the CTA's abort flag and the
+//   warps 8-23  dequant: 8 codes per thread per k-block from the code ring,
+//               scale bytes prefetched from global memory, decoded with
+//               cvt.{e4m3x2,e2m1x2}, written as bf16 into the A tile in the
+//               UMMA K-major 64B-swizzle layout
+// Pipelines (mbarriers): kStages stages of {x tile, W tile}: full_x (TMA
+// bytes), full_w (16 dequant warps), empty (MMA commit); code tiles: cfull
+// (TMA bytes), cempty (16 dequant warps); accumulator: tmem_full (MMA
+// commit), tmem_empty (4 epilogue warps).  TMA / dequant keep prefetching the
+// next tile while the epilogue drains the accumulator.  Every wait is bounded
+// by %globaltimer: a wait that gives up raises the CTA's abort flag and the
 // device error word, and every role then drains its in-flight TMA / MMA work,
 // frees TMEM and returns (the host reads the word with qmm_device_status).
 #include <cuda.h>
@@ -49,14 +53,17 @@ __device__ unsigned int g_device_error = 0;
 namespace {
 
 constexpr int kStages = 4;
-constexpr int kBK = 64;                     // k per stage (128 bytes of bf16: one swizzle row)
+constexpr int kBK = 32;                     // k per stage (64 bytes of bf16: one 64B swizzle row)
 constexpr int kTileW = 128;                 // weight rows per tile (MMA M)
-constexpr int kTileT = 256;                 // tokens per tile (MMA N)
+constexpr int kHalfT = 256;                 // tokens per MMA (MMA N)
+constexpr int kTileT = 2 * kHalfT;          // tokens per tile
 constexpr int kThreads = 768;
-constexpr int kXBytes = kTileT * kBK * 2;   // 32 KB
-constexpr int kWBytes = kTileW * kBK * 2;   // 16 KB
-constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + 32768 /*code ring*/ + 1024 /*align*/ +
-                           512 /*barriers: <= 33 x 8 B + flags*/;
+constexpr int kXHalfBytes = kHalfT * kBK * 2;   // 16 KB
+constexpr int kXBytes = 2 * kXHalfBytes;        // 32 KB
+constexpr int kWBytes = kTileW * kBK * 2;       // 8 KB
+constexpr int kCodeRingBytes = 32768;
+constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + kCodeRingBytes + 1024 /*align*/ +
+                           1024 /*barriers + flags*/;
 constexpr int kDequantWarps = 16;
 constexpr int kEpiWarps = 4;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -114,6 +121,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
         }
     }
 }
+// Bounded wait used on drain paths (no abort check; gives up after the limit).
+__device__ __forceinline__ void mbar_drain(uint64_t* b, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(b, parity) && globaltimer() - t0 < kTimeoutNs) {
+    }
+}
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -158,114 +171,95 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
-// 1024 bytes (SBO), version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// UMMA shared-memory descriptor: K-major, 64-byte swizzle (8-row atoms of
+// 512 bytes, SBO), version 1 (sm_100).  The 16-byte chunk c of row r of a
+// tile sits at r * 64 + ((c ^ ((r >> 1) & 3)) * 16) (tile base 1024-aligned).
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)1 << 16;                    // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;          // SBO
+    d |= (uint64_t)(512 >> 4) << 32;           // SBO: 8 rows x 64 bytes
     d |= (uint64_t)1 << 46;                    // descriptor version
-    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+    d |= (uint64_t)4 << 61;                    // SWIZZLE_64B
     return d;
 }
 
-// kind::f16 instruction descriptor: bf16 A/B, fp32 D, K-major A and B.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileT >> 3) << 17) |
+// kind::f16 instruction descriptor: bf16 A/B, fp32 D, K-major A and B,
+// M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kHalfT >> 3) << 17) |
                             ((uint32_t)(kTileW >> 4) << 24);
 
-// ---- dequantisation of one half k-block (32 codes) of one weight row --------------
-// W code tiles [128 rows x 64 k] arrive by TMA in their own ring (8 KB mxfp8 /
-// 4 KB nvfp4 per stage) with a 64B / 32B swizzle, so the dequant warps' 16-byte
-// reads of 8 consecutive rows hit 8 different bank groups.
+// ---- W code tiles --------------------------------------------------------------
+// [128 rows x 32 k] per k-block, by TMA into their own ring: 32 bytes per row
+// (mxfp8, 32B swizzle: chunk ^= (r >> 2) & 1) or 16 bytes (nvfp4, unswizzled).
 template <int FMT> struct CodeTile;
 template <> struct CodeTile<kMXFP8> {
-    static constexpr int kRowBytes = 64;
-    static constexpr int kStages = 4;
-    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_64B;
-};
-template <> struct CodeTile<kNVFP4> {
     static constexpr int kRowBytes = 32;
-    static constexpr int kStages = 8;
     static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_32B;
 };
-constexpr int kCodeRingBytes = 32768;
-
-struct CodeBuf {
-    uint4 c0, c1;     // fp8: 32 bytes; fp4: c0 = 16 bytes
-    uint32_t s;       // scale byte(s): fp8 one, fp4 two (low byte = first group)
-    int valid;        // codes inside K: 0, 16 or 32
+template <> struct CodeTile<kNVFP4> {
+    static constexpr int kRowBytes = 16;
+    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
 };
 
-// Scale byte of a thread's 16 codes (k [kk, kk + 16) of one row), prefetched
-// ahead from global memory in the checkpoint layout.
+// Scale byte of a thread's 8 codes (k [kk, kk + 8) of one row), prefetched
+// ahead from global memory in the checkpoint layout; 0 outside the matrix.
 template <int FMT>
-__device__ __forceinline__ CodeBuf load_scales(const GemmParams& p, int row, int kk) {
-    CodeBuf b;
-    b.c0 = make_uint4(0, 0, 0, 0);
-    b.c1 = b.c0;
-    b.s = 0;
-    b.valid = 0;
-    if (row >= p.n || kk >= p.k) return b;
-    b.valid = 16;                            // K is a multiple of 16 (the nvfp4 group)
-    const uint8_t* sp = p.scales + (int64_t)row * p.lds;
-    b.s = __ldg(sp + kk / (FMT == kMXFP8 ? 32 : 16));
-    return b;
+__device__ __forceinline__ uint32_t load_scale(const GemmParams& p, int row, int kk) {
+    if (row >= p.n || kk >= p.k) return 0;
+    return __ldg(p.scales + (int64_t)row * p.lds + kk / (FMT == kMXFP8 ? 32 : 16));
 }
 
-// Row r's 16 codes for k quarter q of a swizzled code tile.
+// Row r's 8 codes for k eighth q (codes [8q, 8q + 8) of the k-block).
 template <int FMT>
-__device__ __forceinline__ void read_codes(const uint8_t* tile, int r, int q, CodeBuf& b) {
+__device__ __forceinline__ uint2 read_codes(const uint8_t* tile, int r, int q) {
     if constexpr (FMT == kMXFP8) {
-        const int sw = (r >> 1) & 3;          // SWIZZLE_64B: chunk ^= address bits [7:8]
-        b.c0 = *reinterpret_cast<const uint4*>(tile + r * 64 + ((q ^ sw) << 4));
+        const int sw = (r >> 2) & 1;
+        return *reinterpret_cast<const uint2*>(tile + r * 32 + (((q >> 1) ^ sw) << 4) + (q & 1) * 8);
     } else {
-        const int sw = (r >> 2) & 1;          // SWIZZLE_32B: chunk ^= address bit 7
-        const uint2 v = *reinterpret_cast<const uint2*>(tile + r * 32 + (((q >> 1) ^ sw) << 4) + (q & 1) * 8);
-        b.c0.x = v.x;
-        b.c0.y = v.y;
+        return make_uint2(*reinterpret_cast<const uint32_t*>(tile + r * 16 + 4 * q), 0u);
     }
 }
 
-__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
-    const float2 f = f16x2_to_float2(h);
-    return f32x2_to_bf16x2(f.x, f.y);
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
-// 16 codes -> 2 chunks of 8 bf16 (as uint4), exact.
+// 8 codes -> 8 bf16 (one 16-byte chunk), exact.
 template <int FMT>
-__device__ __forceinline__ void dequant16(const CodeBuf& b, uint4 (&out)[2]) {
+__device__ __forceinline__ uint4 dequant8(uint2 c, uint32_t sbyte) {
     if constexpr (FMT == kMXFP8) {
-        const float s = ue8m0_to_f32(b.s);
-        const uint32_t w[4] = {b.c0.x, b.c0.y, b.c0.z, b.c0.w};
-        uint32_t o[8];
+        const float s = ue8m0_to_f32(sbyte);
+        uint32_t o[4];
+        const uint32_t w[2] = {c.x, c.y};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
             uint32_t h[2];
             e4m3x4_to_f16x2(w[i], h);
-            const float2 a = f16x2_to_float2(h[0]), c = f16x2_to_float2(h[1]);
+            const float2 a = f16x2_to_float2(h[0]), b = f16x2_to_float2(h[1]);
             o[2 * i] = f32x2_to_bf16x2(a.x * s, a.y * s);
-            o[2 * i + 1] = f32x2_to_bf16x2(c.x * s, c.y * s);
+            o[2 * i + 1] = f32x2_to_bf16x2(b.x * s, b.y * s);
         }
-        out[0] = make_uint4(o[0], o[1], o[2], o[3]);
-        out[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        return make_uint4(o[0], o[1], o[2], o[3]);
     } else {
-        // E2M1 x UE4M3 products are exact in f16 (<= 6 significant bits,
-        // magnitudes 2^-10 .. 2688), so the scale is applied with HMUL2.
-        const uint32_t s = e4m3x2_to_f16x2((uint16_t)((b.s & 0xFF) * 0x0101u));
-        const uint32_t w[2] = {b.c0.x, b.c0.y};
+        // An E2M1 value v decodes exactly to f16; moving its exponent and
+        // mantissa fields down by 3 bits gives the bf16 bit pattern of
+        // v * 2^-112 (the f16 exponent field read with bf16's bias; zero
+        // stays zero, E2M1 has no Inf/NaN).  One bf16 multiply by
+        // s * 2^112 then yields v * s exactly (<= 6 significant bits,
+        // magnitudes 2^-10 .. 2688), NaN scales included.
+        const uint16_t sb = f32_to_bf16(ue4m3_to_f32(sbyte) * 0x1p112f);
+        const uint32_t s2 = (uint32_t)sb * 0x10001u;
+        uint32_t h[4], o[4];
+        e2m1x8_to_f16x2(c.x, h);
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            uint32_t h[4];
-            e2m1x8_to_f16x2(w[j], h);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                __half2 v = __hmul2(*reinterpret_cast<__half2*>(&h[i]), *reinterpret_cast<const __half2*>(&s));
-                o[i] = f16x2_to_bf16x2(*reinterpret_cast<uint32_t*>(&v));
-            }
-            out[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t t = ((h[i] & 0x7FFF7FFFu) >> 3) | (h[i] & 0x80008000u);
+            o[i] = bf16x2_mul(t, s2);
         }
+        return make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -273,27 +267,27 @@ template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                 const __grid_constant__ CUtensorMap cmap,
                                                                 GemmParams p) {
-    constexpr int kCStages = CodeTile<FMT>::kStages;
     constexpr int kCBytes = kTileW * CodeTile<FMT>::kRowBytes;   // one code tile
+    constexpr int kCStages = kCodeRingBytes / kCBytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_x = smem;                                   // kStages x 32 KB
-    uint8_t* smem_w = smem + kStages * kXBytes;               // kStages x 16 KB
+    uint8_t* smem_w = smem + kStages * kXBytes;               // kStages x 8 KB
     uint8_t* smem_c = smem_w + kStages * kWBytes;             // kCStages code tiles (32 KB)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_c + kCodeRingBytes);
     uint64_t* full_x = bars;
     uint64_t* full_w = bars + kStages;
     uint64_t* empty = bars + 2 * kStages;
     uint64_t* tmem_full = bars + 3 * kStages;
-    uint64_t* tmem_empty = tmem_full + 2;
-    uint64_t* drain = tmem_empty + 2;
+    uint64_t* tmem_empty = tmem_full + 1;
+    uint64_t* drain = tmem_empty + 1;
     uint64_t* cfull = drain + 1;                              // kCStages
     uint64_t* cempty = cfull + kCStages;                      // kCStages
     volatile int* abort_flag = reinterpret_cast<volatile int*>(cempty + kCStages);
     uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(cempty + kCStages) + 1;
-    static_assert(kStages * (kXBytes + kWBytes) + kCodeRingBytes + (3 * kStages + 5 + 2 * 8) * 8 + 8 + 1024 <=
+    static_assert(kStages * (kXBytes + kWBytes) + kCodeRingBytes + (3 * kStages + 3 + 2 * 16) * 8 + 8 + 1024 <=
                   kSmemBytes, "shared-memory carve-up exceeds the allocation");
-    static_assert(kCStages * kCBytes == kCodeRingBytes, "code ring size");
+    static_assert(kCStages * kCBytes == kCodeRingBytes && kCStages <= 16, "code ring size");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -307,10 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             mbar_init(&cfull[s], 1);
             mbar_init(&cempty[s], kDequantWarps);
         }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(&tmem_full[a], 1);
-            mbar_init(&tmem_empty[a], kEpiWarps);
-        }
+        mbar_init(tmem_full, 1);
+        mbar_init(tmem_empty, kEpiWarps);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -332,9 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
     if (warp == 0) {
         // ---------------- TMA producer (x tiles) ----------------
         if (lane == 0) {
-            int issued_phase[kStages];
-            bool issued[kStages];
-            for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
+            int last = -1;
             for (int it = 0; it < total_kb; ++it) {
                 const int s = it % kStages;
                 const uint32_t ph = (uint32_t)(it / kStages) & 1u;
@@ -344,28 +334,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                 const int tok0 = (t / p.w_tiles) * kTileT;
                 mbar_expect_tx(&full_x[s], kXBytes);
                 tma_load_2d(smem_x + s * kXBytes, &xmap, &full_x[s], kb * kBK, tok0);
-                issued[s] = true;
-                issued_phase[s] = (int)ph;
+                tma_load_2d(smem_x + s * kXBytes + kXHalfBytes, &xmap, &full_x[s], kb * kBK, tok0 + kHalfT);
+                last = it;
             }
             if (!*abort_flag) {
-                // Producer tail: wait until the MMA's last commits to every
-                // stage's empty barrier have landed, so no tensor-core arrive
-                // targets this CTA's shared memory after it exits.
+                // Producer tail: the MMA's last commits to every stage's empty
+                // barrier must land before the CTA exits.
                 for (int it = total_kb; it < total_kb + kStages; ++it) {
                     if (it < kStages) continue;          // stage never used
-                    const int s = it % kStages;
-                    if (!mbar_wait(&empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) break;
+                    if (!mbar_wait(&empty[it % kStages], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) break;
                 }
             }
             if (*abort_flag) {
                 // Let every TMA still in flight land before the CTA exits.
-                for (int s = 0; s < kStages; ++s)
-                    if (issued[s]) {
-                        const uint64_t t0 = globaltimer();
-                        while (!mbar_try_wait(&full_x[s], (uint32_t)issued_phase[s]) &&
-                               globaltimer() - t0 < kTimeoutNs) {
-                        }
-                    }
+                for (int it = max(0, last - kStages + 1); it <= last; ++it)
+                    mbar_drain(&full_x[it % kStages], (uint32_t)(it / kStages) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -374,11 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             int it = 0;
             bool issued_any = false;
             for (int lt = 0; lt < my_tiles && !*abort_flag; ++lt) {
-                const int a = lt & 1;
-                const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
-                if (!mbar_wait(&tmem_empty[a], aph ^ 1u, abort_flag)) break;
+                if (!mbar_wait(tmem_empty, ((uint32_t)lt & 1u) ^ 1u, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(a * kTileT);
                 bool ok = true;
                 for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
                     const int s = it % kStages;
@@ -392,21 +372,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                     const uint32_t wa = smem_u32(smem_w + s * kWBytes);
 #pragma unroll
                     for (int k16 = 0; k16 < kBK / 16; ++k16) {
-                        mma_bf16(d_tmem, sw128_desc(wa + k16 * 32), sw128_desc(xa + k16 * 32), kIdesc,
-                                 (kb > 0 || k16 > 0) ? 1u : 0u);
+                        const uint32_t acc = (kb > 0 || k16 > 0) ? 1u : 0u;
+                        const uint64_t ad = sw64_desc(wa + k16 * 32);
+                        mma_bf16(tmem_base, ad, sw64_desc(xa + k16 * 32), kIdesc, acc);
+                        mma_bf16(tmem_base + kHalfT, ad, sw64_desc(xa + kXHalfBytes + k16 * 32), kIdesc, acc);
                     }
                     issued_any = true;
                     mma_commit(&empty[s]);
                 }
                 if (!ok) break;
-                mma_commit(&tmem_full[a]);
+                mma_commit(tmem_full);
             }
             if (*abort_flag && issued_any) {
                 // Wait (bounded) for every MMA issued so far before TMEM is freed.
                 mma_commit(drain);
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
-                }
+                mbar_drain(drain, 0);
             }
         }
     } else if (warp == 3) {
@@ -426,28 +406,23 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             }
             // Every fill must land before the CTA exits (the dequant warps
             // consume them all on the normal path; bounded on abort).
-            for (int it = max(0, last - kCStages + 1); it <= last; ++it) {
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(&cfull[it % kCStages], (uint32_t)(it / kCStages) & 1u) &&
-                       globaltimer() - t0 < kTimeoutNs) {
-                }
-            }
+            for (int it = max(0, last - kCStages + 1); it <= last; ++it)
+                mbar_drain(&cfull[it % kCStages], (uint32_t)(it / kCStages) & 1u);
         }
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue: TMEM -> bf16 -> y ----------------
         const int q = warp & 3;                     // TMEM lanes 32q .. 32q + 31
         for (int lt = 0; lt < my_tiles; ++lt) {
-            const int a = lt & 1;
-            const uint32_t aph = (uint32_t)(lt >> 1) & 1u;
-            if (!mbar_wait(&tmem_full[a], aph, abort_flag)) break;
+            if (!mbar_wait(tmem_full, (uint32_t)lt & 1u, abort_flag)) break;
             tc_fence_after();
             const int t = (int)blockIdx.x + lt * (int)gridDim.x;
             const int w_row = (t % p.w_tiles) * kTileW + q * 32 + lane;
             const int tok0 = (t / p.w_tiles) * kTileT;
 #pragma unroll 1
             for (int c = 0; c < kTileT / 32; ++c) {
+                if (tok0 + c * 32 >= p.m) break;        // uniform across the warp
                 uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kTileT + c * 32), r);
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
                 if (w_row < p.n) {
                     uint16_t* yp = p.y + (int64_t)(tok0 + c * 32) * p.ldy + w_row;
                     const int tmax = min(32, p.m - (tok0 + c * 32));
@@ -458,51 +433,58 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[a]);
+            if (lane == 0) mbar_arrive(tmem_empty);
         }
     } else if (warp >= 8) {
         // ---------------- dequant: codes -> bf16 A tiles ----------------
-        const int dt = threadIdx.x - 8 * 32;        // 0 .. 511
-        const int r = dt & (kTileW - 1);            // row within the tile
-        const int h = dt >> 7;                      // k quarter: [16h, 16h + 16)
+        // A warp covers 8 rows x 4 k-quarters: the four lanes of a row share
+        // its scale byte (one sector per row), and the warp's code reads and
+        // W-tile writes are contiguous 128 / 256 / 512-byte runs.
+        const int r = (warp - 8) * 8 + (lane >> 2); // row within the tile
+        const int qd = lane & 3;                    // k quarter of the block: codes [8 qd, 8 qd + 8)
         auto coords = [&](int it, int* row, int* kk) {
             const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
             *row = (t % p.w_tiles) * kTileW + r;
-            *kk = (it % p.kblocks) * kBK + 16 * h;
+            *kk = (it % p.kblocks) * kBK + 8 * qd;
         };
-        // Scales are prefetched two k-blocks ahead from global memory; the
-        // codes come from the TMA-filled code ring.
-        CodeBuf cur{}, n1{};
+        // Scale bytes are prefetched four k-blocks ahead.
+        uint32_t sc[4];
         int row, kk;
-        if (total_kb > 0) { coords(0, &row, &kk); cur = load_scales<FMT>(p, row, kk); }
-        if (total_kb > 1) { coords(1, &row, &kk); n1 = load_scales<FMT>(p, row, kk); }
-        // Byte offsets of this thread's 4 swizzled 16-byte chunks in a W tile.
-        const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            sc[i] = 0;
+            if (i < total_kb) {
+                coords(i, &row, &kk);
+                sc[i] = load_scale<FMT>(p, row, kk);
+            }
+        }
+        // This thread's 16-byte bf16 chunk of a W tile row (64B swizzle).
+        const uint32_t w_off = (uint32_t)(r * 64 + ((qd ^ ((r >> 1) & 3)) << 4));
         for (int it = 0; it < total_kb; ++it) {
-            CodeBuf n2 = n1;
-            if (it + 2 < total_kb) { coords(it + 2, &row, &kk); n2 = load_scales<FMT>(p, row, kk); }
+            const uint32_t cur = sc[0];
+            sc[0] = sc[1];
+            sc[1] = sc[2];
+            sc[2] = sc[3];
+            sc[3] = 0;
+            if (it + 4 < total_kb) {
+                coords(it + 4, &row, &kk);
+                sc[3] = load_scale<FMT>(p, row, kk);
+            }
             const int s = it % kStages;
             const uint32_t ph = (uint32_t)(it / kStages) & 1u;
             const int cs = it % kCStages;
             if (!mbar_wait(&cfull[cs], (uint32_t)(it / kCStages) & 1u, abort_flag)) break;
-            read_codes<FMT>(smem_c + cs * kCBytes, r, h, cur);
-            uint4 o[2];
-            dequant16<FMT>(cur, o);
+            const uint2 codes = read_codes<FMT>(smem_c + cs * kCBytes, r, qd);
             __syncwarp();
             if (lane == 0) mbar_arrive(&cempty[cs]);
-            if (cur.valid == 0) o[0] = o[1] = make_uint4(0, 0, 0, 0);   // rows >= N, k >= K
+            // Codes outside the matrix are zero (TMA fill) and their scale
+            // byte reads as 0, so the chunk is exactly zero.
+            const uint4 o = dequant8<FMT>(codes, cur);
             if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-            uint8_t* wt = smem_w + s * kWBytes + row_off;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int chunk = (2 * h + j) ^ (r & 7);
-                *reinterpret_cast<uint4*>(wt + chunk * 16) = o[j];
-            }
+            *reinterpret_cast<uint4*>(smem_w + s * kWBytes + w_off) = o;
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_w[s]);
-            cur = n1;
-            n1 = n2;
         }
     }
 
@@ -531,7 +513,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int FMT>
 int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int grid, cudaStream_t stream) {
     // Code tiles: u8 [N rows, K*bits/8 bytes] with row stride ldc, box
-    // [128 rows x 64 k], swizzled to match read_codes().
+    // [128 rows x 32 k], swizzled to match read_codes().
     CUtensorMap cmap;
     const cuuint64_t cdim[2] = {(cuuint64_t)(a.k * (FMT == kMXFP8 ? 8 : 4) / 8), (cuuint64_t)a.n};
     const cuuint64_t cstride[1] = {(cuuint64_t)a.ldc};
@@ -558,12 +540,11 @@ int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, in
 
 int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     *handled = false;
-    // Envelope: 16-byte aligned x rows for TMA, 16-byte aligned code rows for
-    // the dequant warps' vector loads, 32-bit indices.
+    // Envelope: 16-byte aligned x rows and code rows (TMA), 32-bit indices.
     const auto x_addr = reinterpret_cast<uintptr_t>(a.x);
     const auto c_addr = reinterpret_cast<uintptr_t>(a.codes);
     if ((x_addr & 15) || ((a.ldx * 2) & 15) || (c_addr & 15) || (a.ldc & 15)) return QMM_OK;
-    if (a.m > INT32_MAX || a.n > INT32_MAX || a.k > INT32_MAX || a.m < 1) return QMM_OK;
+    if (a.m > INT32_MAX - kTileT || a.n > INT32_MAX || a.k > INT32_MAX || a.m < 1) return QMM_OK;
     auto encode = encode_fn();
     if (!encode) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     int dev = 0;
@@ -572,13 +553,14 @@ int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     if (int rc = device_info(dev, &info)) return rc;
     if (info.smem_optin < (size_t)kSmemBytes) return QMM_OK;
 
+    // x tiles: bf16 [M rows, K] with row stride ldx, box [256 rows x 32 k], 64B swizzle.
     CUtensorMap map;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
     const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTileT};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kHalfT};
     const cuuint32_t estride[2] = {1, 1};
     CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box,
-                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
 
