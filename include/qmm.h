@@ -131,6 +131,30 @@ int qmm_quantized_matmul(void* y_dev, int64_t ldy,
                          qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
                          void* stream);
 
+/* Same arguments, result (within the parity tolerance) and errors as
+ * qmm_quantized_matmul, for callers that may not allocate device memory.  No
+ * counterpart in the reference.  For M <= 8 it runs the tensor-core decode
+ * kernel of qmm_run on the checkpoint-layout weights, with that kernel's
+ * scratch (per-unit scale tiles, stream-K partial sums, counters) in one
+ * static 8 MiB device array per device; cudaMalloc/cudaFree are never called.
+ * A weight whose scratch exceeds 8 MiB fails with QMM_ERR_OUT_OF_MEMORY: the
+ * scale tiles take N*K/16 (nvfp4) or N*K/32 (mxfp8) bytes and the partial
+ * sums 1.2 MB, so N*K up to about 110 M (nvfp4) or 220 M (mxfp8) fits, e.g.
+ * [5120, 17408] and [17408, 5120].  Other shapes take the
+ * scratch-free kernels of qmm_quantized_matmul.
+ *   - the first call on each device looks up the array's address
+ *     (cudaGetSymbolAddress): make it before any stream capture begins;
+ *   - calls that overlap in time on one device share the array and race:
+ *     order them on one stream;
+ *   - the array keeps the last call's contents after it returns. */
+int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy,
+                                 const void* x_dev, int64_t m, int64_t k, int64_t ldx,
+                                 const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
+                                 const uint8_t* scales_dev, int64_t s_rows, int64_t s_cols,
+                                 const void* biases, bool transpose,
+                                 qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
+                                 void* stream);
+
 /* ---- resident weights (src/weights.zig:203-353 + src/model.zig:244) ----- */
 
 #define QMM_SRC_HOST   0  /* codes/scales pointers are host memory */

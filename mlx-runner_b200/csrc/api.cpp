@@ -213,6 +213,52 @@ extern "C" int qmm_quantized_matmul(void* y_dev, int64_t ldy, const void* x_dev,
     return dispatch(a, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy, const void* x_dev, int64_t m, int64_t k,
+                                            int64_t ldx, const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
+                                            const uint8_t* scales_dev, int64_t s_rows, int64_t s_cols,
+                                            const void* biases, bool transpose, qmm_optional_int group_size,
+                                            qmm_optional_int bits, const char* mode, void* stream) {
+    QMM_FAULT_POINT("qmm_quantized_matmul_noalloc");
+    qmm_quant_spec spec;
+    if (int rc = qmm_spec_from_args(group_size, bits, mode, &spec)) return rc;
+    if (biases) return set_error(QMM_ERR_BAD_ARGUMENT, "%s takes no biases", mode);
+    if (!transpose) return set_error(QMM_ERR_BAD_ARGUMENT, "only transpose=true (W [N, K]) is supported");
+    if (k <= 0 || k % spec.group_size)
+        return set_error(QMM_ERR_BAD_SHAPE, "k=%lld is not a positive multiple of group %d", (long long)k, spec.group_size);
+    if (w_rows < 0 || w_rows != s_rows)
+        return set_error(QMM_ERR_BAD_SHAPE, "w rows %lld != scales rows %lld", (long long)w_rows, (long long)s_rows);
+    if (w_cols * 32 / spec.bits != k || (w_cols * 32) % spec.bits)
+        return set_error(QMM_ERR_BAD_SHAPE, "w cols %lld do not pack k=%lld at %d bits", (long long)w_cols,
+                         (long long)k, spec.bits);
+    if (s_cols * spec.group_size != k)
+        return set_error(QMM_ERR_BAD_SHAPE, "scales cols %lld != k/group = %lld", (long long)s_cols,
+                         (long long)(k / spec.group_size));
+    const int64_t n = w_rows;
+    if (int rc = check_xy(x_dev, m, k, ldx, y_dev, n, ldy)) return rc;
+    if (m == 0 || n == 0) return QMM_OK;
+    if (!w_dev || !scales_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "w or scales is NULL");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    QmmArgs a;
+    a.fmt = format_of(spec);
+    a.codes = reinterpret_cast<const uint8_t*>(w_dev);
+    a.ldc = w_cols * 4;
+    a.scales = scales_dev;
+    a.lds = s_cols;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(y_dev);
+    a.ldy = ldy;
+    a.m = m; a.n = n; a.k = k;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bool handled = false;
+    if (int rc = launch_gemv_tc_static(a, s, &handled)) return rc;
+    if (handled) return QMM_OK;
+    // Outside the decode kernel's envelope (M > 8, unaligned rows): the
+    // scratch-free kernels of qmm_quantized_matmul.
+    return dispatch(a, s);
+}
+
 extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t n, int64_t k, int64_t ldw,
                                  int64_t lds, qmm_quant_spec spec, int src_kind, void* stream,
                                  qmm_weight** out) {

@@ -665,4 +665,132 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     return QMM_OK;
 }
 
+// ---- static-scratch variant (allocates nothing) ------------------------------------
+//
+// The same decode kernel run on the caller's packed weights in the checkpoint
+// layout, with every scratch buffer (per-unit scale tiles, stream-K partial
+// sums, row-block counters) carved from one file-scope device array instead
+// of per-weight allocations.  The array's address is looked up once per
+// device (cudaGetSymbolAddress, that device current).  Calls that overlap in
+// time on one device share the array and race; after a call the array keeps
+// that call's contents.
+
+namespace {
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
+__device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+int static_scratch_base(int dev, uint8_t** base) {
+    static std::mutex mu;
+    static uint8_t* addr[64] = {};
+    if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(static scratch)");
+        addr[dev] = static_cast<uint8_t*>(p);
+    }
+    *base = addr[dev];
+    return QMM_OK;
+}
+}  // namespace
+
+int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) {
+    *handled = false;
+    if (a.yf || a.m < 1 || a.m > kXRows) return QMM_OK;
+    if (a.n <= 0 || a.n > INT32_MAX || a.k > INT32_MAX) return QMM_OK;
+    // TMA envelope: 16-byte aligned x and code rows.
+    const auto xa = reinterpret_cast<uintptr_t>(a.x), ca = reinterpret_cast<uintptr_t>(a.codes);
+    if ((xa & 15) || ((a.ldx * 2) & 15) || (ca & 15) || (a.ldc & 15)) return QMM_OK;
+    auto enc = encoder();
+    if (!enc) return QMM_OK;
+    int dev = 0;
+    QMM_CUDA_TRY(cudaGetDevice(&dev));
+    DeviceInfo info;
+    if (int rc = device_info(dev, &info)) return rc;
+    if (info.smem_optin < (size_t)smem_bytes<kNVFP4>()) return QMM_OK;
+
+    const int fmt = a.fmt;
+    const int KC = fmt == kMXFP8 ? Cfg<kMXFP8>::KC : Cfg<kNVFP4>::KC;
+    const int SB = fmt == kMXFP8 ? Cfg<kMXFP8>::SB : Cfg<kNVFP4>::SB;
+    const int group = fmt == kMXFP8 ? 32 : 16;
+    const int64_t kchunks = (a.k + KC - 1) / KC, row_blocks = (a.n + kRows - 1) / kRows;
+    const int64_t units = kchunks * row_blocks;
+    const int64_t grid = std::min<int64_t>(units, info.sms);
+    auto align256 = [](int64_t v) { return (v + 255) / 256 * 256; };
+    const int64_t tiled_bytes = units * kRows * SB;
+    const int64_t partial_off = align256(tiled_bytes);
+    const int64_t counters_off = align256(partial_off + grid * 2 * kRows * 8 * (int64_t)sizeof(float));
+    const int64_t need = counters_off + row_blocks * (int64_t)sizeof(unsigned int);
+    if (need > (int64_t)kStaticScratchBytes)
+        return set_error(QMM_ERR_OUT_OF_MEMORY,
+                         "[%lld, %lld] weight needs %lld bytes of static scratch; the maximum is %zu (8 MiB)",
+                         (long long)a.n, (long long)a.k, (long long)need, kStaticScratchBytes);
+    uint8_t* base = nullptr;
+    if (int rc = static_scratch_base(dev, &base)) return rc;
+
+    CUtensorMap cmap, xmap;
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)(a.k * (fmt == kMXFP8 ? 8 : 4) / 8), (cuuint64_t)a.n};
+        const cuuint64_t gstride[1] = {(cuuint64_t)a.ldc};
+        const cuuint32_t box[2] = {128, (cuuint32_t)kRows};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.codes), gdim, gstride, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return QMM_OK;
+    }
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
+        const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
+        const cuuint32_t box[2] = {256u, (cuuint32_t)kXRows};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return QMM_OK;
+    }
+
+    // The counters must start at zero (a call that gave up a wait can leave
+    // them set); the scale tiles are rebuilt from the checkpoint layout.
+    unsigned int* counters = reinterpret_cast<unsigned int*>(base + counters_off);
+    QMM_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)row_blocks * sizeof(unsigned int), stream));
+    const unsigned rgrid = (unsigned)std::min<int64_t>((tiled_bytes + 255) / 256, (int64_t)info.sms * 8);
+    retile_scales_kernel<<<rgrid, 256, 0, stream>>>(a.scales, a.lds, (int)a.n, (int)(a.k / group), (int)kchunks,
+                                                    (int)row_blocks, SB, base);
+    QMM_CUDA_TRY(cudaGetLastError());
+
+    TcParams p;
+    p.scales_tiled = base;
+    p.y = a.y;
+    p.partial = reinterpret_cast<float*>(base + partial_off);
+    p.counters = counters;
+    p.ldy = a.ldy;
+    p.m = (int)a.m;
+    p.n = (int)a.n;
+    p.k = (int)a.k;
+    p.kchunks = (int)kchunks;
+    p.row_blocks = (int)row_blocks;
+    p.units = (int)units;
+    static bool configured[2][64] = {};
+    if (fmt == kMXFP8) {
+        if (!configured[0][dev]) {
+            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kMXFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              smem_bytes<kMXFP8>()));
+            configured[0][dev] = true;
+        }
+        qmm_gemv_tc_kernel<kMXFP8><<<(unsigned)grid, kThreads, smem_bytes<kMXFP8>(), stream>>>(cmap, xmap, p);
+    } else {
+        if (!configured[1][dev]) {
+            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kNVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              smem_bytes<kNVFP4>()));
+            configured[1][dev] = true;
+        }
+        qmm_gemv_tc_kernel<kNVFP4><<<(unsigned)grid, kThreads, smem_bytes<kNVFP4>(), stream>>>(cmap, xmap, p);
+    }
+    QMM_CUDA_TRY(cudaGetLastError());
+    *handled = true;
+    return QMM_OK;
+}
+
 }  // namespace qmm

@@ -83,6 +83,9 @@ struct GemvTcState;
 int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream);
 void gemv_tc_release(qmm_weight* w);
 int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, bool* handled);
+// The same kernel on checkpoint-layout weights with its scratch in a static
+// device array (no allocation); errors if the weight needs more than it holds.
+int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled);
 // Read and clear the kernel's device-side timeout word (synchronizes s).
 cudaError_t gemv_tc_take_error(unsigned int* v, cudaStream_t s);
 

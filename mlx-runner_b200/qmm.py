@@ -40,7 +40,7 @@ SRC_HOST, SRC_DEVICE = 0, 1
 # Every symbol the C ABI (include/qmm.h) exports.
 EXPORTS = (
     "qmm_abi_version", "qmm_infer_quant_spec", "qmm_mode_str", "qmm_spec_from_args",
-    "qmm_quantized_matmul", "qmm_weight_create", "qmm_weight_create_shard", "qmm_shard_range",
+    "qmm_quantized_matmul", "qmm_quantized_matmul_noalloc", "qmm_weight_create", "qmm_weight_create_shard", "qmm_shard_range",
     "qmm_weight_destroy",
     "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
     "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
@@ -99,6 +99,7 @@ def lib() -> ctypes.CDLL:
     L.qmm_spec_from_args.argtypes = [OptionalInt, OptionalInt, ctypes.c_char_p, ctypes.POINTER(QuantSpec)]
     L.qmm_quantized_matmul.argtypes = [vp, i64, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp,
                                        ctypes.c_bool, OptionalInt, OptionalInt, ctypes.c_char_p, vp]
+    L.qmm_quantized_matmul_noalloc.argtypes = L.qmm_quantized_matmul.argtypes
     L.qmm_weight_create.argtypes = [vp, vp, i64, i64, i64, i64, QuantSpec, i32, vp, ctypes.POINTER(vp)]
     L.qmm_weight_create_shard.argtypes = [vp, vp, i64, i64, QuantSpec, i32, i32, i32, i32, vp,
                                           ctypes.POINTER(vp)]
@@ -234,6 +235,25 @@ def quantized_matmul(x, w, scales, biases=None, transpose: bool = True, group_si
         None if biases is None else biases.data_ptr(), transpose, OptionalInt.of(group_size),
         OptionalInt.of(bits), mode.encode(), _stream_handle(stream)))
     return y.reshape(*x.shape[:-1], n) if out is None else y
+
+
+def quantized_matmul_noalloc(x, w, scales, out, biases=None, transpose: bool = True,
+                             group_size: Optional[int] = None, bits: Optional[int] = None, mode: str = "mxfp8",
+                             stream=None):
+    """quantized_matmul into the caller's `out` through the entry point that
+    allocates no device memory (its scratch is a static device array; calls
+    that overlap on one device race)."""
+    torch = _torch()
+    if x.dtype != torch.bfloat16:
+        raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+    x2 = _as_2d(x)
+    m, k = x2.shape
+    check(lib().qmm_quantized_matmul_noalloc(
+        out.data_ptr(), out.stride(0), x2.data_ptr(), m, k, x2.stride(0),
+        w.data_ptr(), w.shape[0], w.shape[1], scales.data_ptr(), scales.shape[0], scales.shape[1],
+        None if biases is None else biases.data_ptr(), transpose, OptionalInt.of(group_size),
+        OptionalInt.of(bits), mode.encode(), _stream_handle(stream)))
+    return out
 
 
 @dataclass
