@@ -45,10 +45,10 @@ M_SET = (1, 2, 3, 4)
 GROUP, BITS = 16, 4
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-# Per-launch DRAM traffic of the GEMV kernel (dram__bytes_read.sum +
+# Per-launch DRAM traffic of the decode kernel (dram__bytes_read.sum +
 # dram__bytes_write.sum) from the ncu capture summarised in
-# profiles/gemv_nvfp4_k17408_n5120.md; None until that capture exists.
-GEMV_TRAFFIC_BYTES = None
+# profiles/qmm_gemv_tc_nvfp4_k17408_n5120.md (50.22 MB read + 0.06 MB written).
+GEMV_TRAFFIC_BYTES = 50.28e6
 
 
 def _load(name, path):
@@ -212,7 +212,8 @@ def prefill_measure(args, qmm, oracle, dev, world: int, rank: int, barrier, max_
     wt.close()
     return {"workload": f"cfg3: nvfp4 prefill GEMM x [{m}, {k}] . W[{n}, {k}]^T, N-sharded over {world} GPU(s)",
             "metric": "TFLOP/s", "value": tflops, "ms_per_gemm": ms, "steps": args.prefill_steps,
-            "l2": "inputs larger than L2 (x 335 MB)",
+            "l2": f"x {m * k * 2 / 1e6:.0f} MB + W {wt.n * k * 9 / 16 / 1e6:.0f} MB streamed per GEMM "
+                  f"({'larger' if m * k * 2 > L2_BYTES else 'not larger'} than L2)",
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                          "frac": per_gpu / peak, "peak_kind": kind, "kernel": "qmm_gemm_kernel<nvfp4>",
                          "note": "dense bf16 MMA peak: W is dequantised exactly to bf16 (parity); "
