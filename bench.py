@@ -46,8 +46,8 @@ GROUP, BITS = 16, 4
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 # Per-launch DRAM traffic of the decode kernel (dram__bytes_read.sum +
-# dram__bytes_write.sum) from the ncu capture summarised in
-# profiles/qmm_gemv_tc_nvfp4_k17408_n5120.md (50.22 MB read + 0.06 MB written).
+# dram__bytes_write.sum) from an ncu --set full capture of two launches of
+# this bench's decode run (50.22 MB read + 0.06 MB written per launch).
 GEMV_TRAFFIC_BYTES = 50.28e6
 
 
@@ -261,6 +261,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (profiling runs)")
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of load before warm-up (clock samples)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA-graph replays")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM (profiling runs)")
     ap.add_argument("--prefill-m", type=int, default=PREFILL["m"])
     ap.add_argument("--prefill-steps", type=int, default=5)
@@ -327,10 +328,11 @@ def main() -> None:
     stream = torch.cuda.current_stream()
 
     def gemm(wt, m):
+        cur = torch.cuda.current_stream()     # the capture stream inside a graph capture
         if comm is None:
-            wt.run(x_dev[m], out=y_dev[m], stream=stream)
+            wt.run(x_dev[m], out=y_dev[m], stream=cur)
         else:
-            comm.run_rowparallel(wt, x_dev[m], out=y_dev[m], stream=stream)
+            comm.run_rowparallel(wt, x_dev[m], out=y_dev[m], stream=cur)
 
     def step():
         for wt in weights:
@@ -338,37 +340,74 @@ def main() -> None:
                 gemm(wt, m)
 
     launches_per_gemm = 1 if comm is None else 2   # GEMV (+ fp32->bf16 after the all-reduce)
+
+    # One step (and, for the kernel-alone timing, one pass per M) is replayed
+    # as a CUDA graph, as a decode loop runs it: the device time then excludes
+    # host launch gaps.  The NCCL path (world > 1) runs eagerly.
+    graphs = {}
+    launch_mode = "eager"
+    if world == 1 and not args.eager:
+        try:
+            cap = torch.cuda.Stream()
+            cap.wait_stream(stream)
+            with torch.cuda.stream(cap):
+                step()                          # settles per-weight launch state outside capture
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                step()
+            graphs["step"] = g
+            for m in M_SET:
+                gm = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gm, stream=cap):
+                    for wt in weights:
+                        wt.run(x_dev[m], out=y_dev[m], stream=cap)
+                graphs[m] = gm
+            torch.cuda.synchronize()
+            launch_mode = "cuda_graph"
+        except Exception as exc:  # capture unsupported here: time eager launches
+            graphs = {}
+            print(f"bench: graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+
+    def run_step():
+        if graphs:
+            graphs["step"].replay()
+        else:
+            step()
+
     sampler = ClockSampler(local)
     with sampler:
         # Sustained load so the clock samples see the same work as the timed region.
         barrier()
         t_soak = time.perf_counter()
         while time.perf_counter() - t_soak < args.soak:
-            step()
+            run_step()
             torch.cuda.synchronize()
         for _ in range(args.warmup):
-            step()
+            run_step()
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            run_step()
         ev1.record(stream)
         barrier()
         ms = max_over_ranks(ev0.elapsed_time(ev1))
 
-        # Kernel-alone timing of the dominant kernel (events on its stream,
-        # around every launch of one timed pass).
-        kev = []
-        for wt in weights:
-            for m in M_SET:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                wt.run(x_dev[m], out=y_dev[m], stream=stream)
-                b.record(stream)
-                kev.append((m, a, b))
-        torch.cuda.synchronize()
-        k_ms = [(m, a.elapsed_time(b)) for m, a, b in kev]
+        # Kernel-alone timing of the dominant kernel (events on its stream):
+        # one pass of `copies` launches per M, averaged per launch.
+        k_ms = []
+        for m in M_SET:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            if graphs:
+                graphs[m].replay()
+            else:
+                for wt in weights:
+                    wt.run(x_dev[m], out=y_dev[m], stream=stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            k_ms.extend([(m, a.elapsed_time(b) / copies)] * copies)
 
     # e2e: host buffers through the C ABI, copies inside the timed region.
     x_host = {m: x_full[m][:, rank * k_shard:(rank + 1) * k_shard].contiguous().pin_memory() for m in M_SET}
@@ -408,6 +447,7 @@ def main() -> None:
     peak, peak_kind = peaks()
     clocks = sampler.summary()
 
+    graphs.clear()
     for wt in weights:
         wt.close()
     weights = []
@@ -422,6 +462,7 @@ def main() -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4xbf16->f32acc",
             "data": "synthetic (seeded N(0,1) x, N(0,0.02^2) W quantized by the oracle's NVFP4 rule)",
             "config": dict(CONFIG, copies=copies, parallelism=f"tp{world} (K-shard)" if world > 1 else "none",
+                           launch=launch_mode,
                            l2=f"inputs larger than L2: {copies} weight copies x {shard_bytes / 1e6:.1f} MB rotate"),
             "tflops": step_flops(copies) * args.steps / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -51,8 +51,10 @@ constexpr int kStages = 4;
 constexpr int kBox = kRows * 128;          // one 2D TMA box: 128 rows x 128 code bytes
 constexpr int kCodeBytes = 2 * kBox;       // 32 KB: 256 code bytes per row per unit
 constexpr int kXRows = 8;                  // x rows staged per unit (M padded to 8)
+constexpr int kConverters = 4;             // x-converter warps (tokens m = v, v + 4)
 constexpr int kConsumers = 16;             // 8 row groups x 2 k halves
-constexpr int kThreads = (2 + kConsumers) * 32;  // producer, converter, consumers
+constexpr int kFirstConsumer = 1 + kConverters;  // warp index of consumer 0
+constexpr int kThreads = (1 + kConverters + kConsumers) * 32;  // producer, converters, consumers
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 template <int FMT> struct Cfg;
@@ -171,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&xready[s], 1);
+            mbar_init(&xready[s], kConverters);
             mbar_init(&empty[s], kConsumers);
         }
         *abort_flag = 0;
@@ -205,14 +207,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 }
             }
         }
-    } else if (warp == 1) {
-        // ---------------- x converter ----------------
-        // B-fragment slots of x rows >= M are zero for the whole launch and
-        // their x-scale factors 1 (their accumulator columns are never stored).
-        for (int off = lane * 16; off < kStages * kXfBytes; off += 32 * 16)
+    } else if (warp < kFirstConsumer) {
+        // ---------------- x converters ----------------
+        // Warp cv converts x rows m = cv, cv + 4 (m < M).  B-fragment slots of x
+        // rows >= M are zero for the whole launch and their x-scale factors 1
+        // (their accumulator columns are never stored).
+        const int cv = warp - 1, ct = threadIdx.x - 32;
+        for (int off = ct * 16; off < kStages * kXfBytes; off += kConverters * 32 * 16)
             *reinterpret_cast<uint4*>(s_xf + off) = make_uint4(0, 0, 0, 0);
-        for (int t = lane; t < kStages * 8; t += 32) s_xs[t] = 1.0f;
-        __syncwarp();
+        for (int t = ct; t < kStages * 8; t += kConverters * 32) s_xs[t] = 1.0f;
+        named_sync(2, kConverters * 32);
         for (int i = 0; i < nunits; ++i) {
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)(i / kStages) & 1u;
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             uint8_t* xf = s_xf + s * kXfBytes;
             const int k0 = E * lane;
             const uint16_t* rbase = raw + (k0 >> 8) * (kXRows * 256) + (k0 & 255);
-            for (int m = 0; m < p.m; ++m) {
+            for (int m = cv; m < p.m; m += kConverters) {
                 float v[E];
                 uint32_t w[E / 2];
 #pragma unroll
@@ -289,11 +293,23 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         // ---------------- consumers ----------------
         // Warp cw owns rows [16 rg, 16 rg + 16) of every unit (rg = cw % 8)
         // over one half of the unit's k range (kh = cw / 8).
-        const int cw = warp - 2, rg = cw & 7, kh = cw >> 3;
+        const int cw = warp - kFirstConsumer, rg = cw & 7, kh = cw >> 3;
         const int g = lane >> 2, c = lane & 3;
         const int r0 = 16 * rg + g, r1 = r0 + 8;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
+        // Static schedule: CTA j owns units [first_unit(j), first_unit(j + 1));
+        // unit u belongs to CTA owner(u).  32-bit division when the products
+        // fit (64-bit division is a long software sequence).
+        const unsigned G = gridDim.x;
+        const bool fits32 = (uint64_t)(p.units + 1) * G < (1ull << 32);
+        auto first_unit = [&](int j) -> int {
+            return fits32 ? (int)(((unsigned)p.units * (unsigned)j) / G) : (int)(((int64_t)p.units * j) / G);
+        };
+        auto owner = [&](int u) -> int {
+            return fits32 ? (int)(((unsigned)(u + 1) * G - 1u) / (unsigned)p.units)
+                          : (int)(((int64_t)(u + 1) * G - 1) / p.units);
+        };
         auto flush = [&](int rb, bool complete) {
             // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
             // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
@@ -329,18 +345,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             // for every thread past the next barrier.  (One fence per CTA:
             // fences by every thread stall for microseconds under HBM load.)
             named_sync(1, kConsumers * 32);
-            if (threadIdx.x == 64) {
-                // CTAs covering rb: i_first .. i_last (static schedule).
-                const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
-                const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
-                const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
-                __threadfence();
-                const unsigned prev = atomicAdd(&p.counters[rb], 1u);
+            if (threadIdx.x == kFirstConsumer * 32) {
+                // CTAs covering rb: owner(first unit) .. owner(last unit).  The
+                // acq_rel add releases this CTA's partial (ordered before it by
+                // the barrier) and, for the last arriver, acquires the others'.
+                const int ifirst = owner(rb * p.kchunks), ilast = owner(rb * p.kchunks + p.kchunks - 1);
+                unsigned prev;
+                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                             : "=r"(prev) : "l"(p.counters + rb) : "memory");
                 const int last = (prev == (unsigned)(ilast - ifirst)) ? 1 : 0;
-                if (last) {
-                    __threadfence();
-                    p.counters[rb] = 0;
-                }
+                if (last) p.counters[rb] = 0;
                 *s_last = last;
             }
             named_sync(1, kConsumers * 32);
@@ -348,10 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 // Sum the contributors' partials in CTA order.  Each of the 512
                 // consumer threads owns 2 of the block's 128 x 8 outputs and
                 // keeps 8 contributor loads in flight per batch.
-                const int ua = rb * p.kchunks, ub = ua + p.kchunks - 1;
-                const int ifirst = (int)(((int64_t)(ua + 1) * gridDim.x - 1) / p.units);
-                const int ilast = (int)(((int64_t)(ub + 1) * gridDim.x - 1) / p.units);
-                const int t = threadIdx.x - 64;
+                const int ifirst = owner(rb * p.kchunks), ilast = owner(rb * p.kchunks + p.kchunks - 1);
+                const int t = threadIdx.x - kFirstConsumer * 32;
                 float v[2] = {0.f, 0.f};
                 for (int j0 = ifirst; j0 <= ilast; j0 += 8) {
                     float ld[8][2];
@@ -360,8 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const int j = j0 + q;
                         ld[q][0] = ld[q][1] = 0.f;
                         if (j <= ilast) {
-                            const int ju0 = (int)(((int64_t)p.units * j) / gridDim.x);
-                            const int jslot = (ju0 / p.kchunks == rb) ? 0 : 1;
+                            const int jslot = (first_unit(j) / p.kchunks == rb) ? 0 : 1;
                             const float* src = p.partial + ((int64_t)j * 2 + jslot) * kRows * 8;
                             ld[q][0] = __ldcg(src + t);
                             ld[q][1] = __ldcg(src + t + 512);
