@@ -34,6 +34,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "formats.cuh"
@@ -180,23 +181,39 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // A dependent grid (the next decode call) may start on SMs this grid frees.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            int last = -1;
-            for (int i = 0; i < nunits; ++i) {
-                const int s = i % kStages;
-                const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-                const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
+            // Weight bytes of a unit (codes + scales) and its x chunk.
+            auto issue_w = [&](int i) {
+                const int s = i % kStages, u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
                 mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes + kXRawBytes);
                 tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 256, rb * kRows);
                 tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], kc * 256 + 128, rb * kRows);
                 bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)u * kScaleBytes, kScaleBytes, &full[s]);
+            };
+            auto issue_x = [&](int i) {
+                const int s = i % kStages, kc = (u0 + i) % p.kchunks;
 #pragma unroll
                 for (int xb = 0; xb < KC / 256; ++xb)   // x rows of the chunk, 256 elements per box
                     tma_2d(s_xraw + s * kXRawBytes + xb * kXRows * 512, &xmap, &full[s], kc * KC + 256 * xb, 0);
+            };
+            // The first ring of weight tiles streams before the wait on the
+            // previous grid (programmatic dependent launch): only x (and the
+            // outputs, written after x is consumed) depend on earlier kernels.
+            const int pre = min(kStages, nunits);
+            for (int i = 0; i < pre; ++i) issue_w(i);
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; i < pre; ++i) issue_x(i);
+            int last = pre - 1;
+            for (int i = pre; i < nunits; ++i) {
+                const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+                if (!mbar_wait(&empty[i % kStages], ph ^ 1u, abort_flag)) break;
+                issue_w(i);
+                issue_x(i);
                 last = i;
             }
             // Drain: every stage's last fill must land, and every consumer
@@ -656,20 +673,39 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     p.units = st->kchunks * st->row_blocks;
     static bool configured[2][64] = {};
     int dev = w->device;
+    // Programmatic dependent launch: the kernel may start while the previous
+    // kernel on the stream finishes; it streams its first weight tiles, then
+    // waits (griddepcontrol.wait) before reading x or writing anything.
+    // QMM_NO_PDL=1 launches in plain stream order.
+    static const bool pdl = [] {
+        const char* e = getenv("QMM_NO_PDL");
+        return !(e && e[0] == '1');
+    }();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)st->grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
     if (fmt == kMXFP8) {
         if (dev < 64 && !configured[0][dev]) {
             QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kMXFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               smem_bytes<kMXFP8>()));
             configured[0][dev] = true;
         }
-        qmm_gemv_tc_kernel<kMXFP8><<<st->grid, kThreads, smem_bytes<kMXFP8>(), stream>>>(st->cmap, xmap, p);
+        cfg.dynamicSmemBytes = smem_bytes<kMXFP8>();
+        QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_gemv_tc_kernel<kMXFP8>, st->cmap, xmap, p));
     } else {
         if (dev < 64 && !configured[1][dev]) {
             QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kNVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               smem_bytes<kNVFP4>()));
             configured[1][dev] = true;
         }
-        qmm_gemv_tc_kernel<kNVFP4><<<st->grid, kThreads, smem_bytes<kNVFP4>(), stream>>>(st->cmap, xmap, p);
+        cfg.dynamicSmemBytes = smem_bytes<kNVFP4>();
+        QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_gemv_tc_kernel<kNVFP4>, st->cmap, xmap, p));
     }
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;
