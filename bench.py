@@ -343,31 +343,44 @@ def main() -> None:
 
     # One step (and, for the kernel-alone timing, one pass per M) is replayed
     # as a CUDA graph, as a decode loop runs it: the device time then excludes
-    # host launch gaps.  The NCCL path (world > 1) runs eagerly.
+    # host launch gaps.  With world > 1 the graphs hold the NCCL all-reduces;
+    # every rank uses graphs only if every rank captured them.
+    def capture() -> dict:
+        # Graphs live only in the returned dict (no other references), so
+        # clearing it releases them - graphs holding NCCL calls must be gone
+        # before the communicators are destroyed.
+        out = {}
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            step()                              # settles per-weight launch state outside capture
+        torch.cuda.synchronize()
+        out["step"] = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(out["step"], stream=cap):
+            step()
+        for m in M_SET:
+            out[m] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(out[m], stream=cap):
+                for wt in weights:
+                    gemm(wt, m)
+        torch.cuda.synchronize()
+        return out
+
     graphs = {}
     launch_mode = "eager"
-    if world == 1 and not args.eager:
+    if not args.eager:
         try:
-            cap = torch.cuda.Stream()
-            cap.wait_stream(stream)
-            with torch.cuda.stream(cap):
-                step()                          # settles per-weight launch state outside capture
-            torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
-                step()
-            graphs["step"] = g
-            for m in M_SET:
-                gm = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gm, stream=cap):
-                    for wt in weights:
-                        wt.run(x_dev[m], out=y_dev[m], stream=cap)
-                graphs[m] = gm
-            torch.cuda.synchronize()
+            graphs = capture()
             launch_mode = "cuda_graph"
         except Exception as exc:  # capture unsupported here: time eager launches
             graphs = {}
             print(f"bench: graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+        if world > 1:
+            ok = torch.tensor([1.0 if graphs else 0.0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if ok.item() < 1.0:
+                graphs = {}
+                launch_mode = "eager"
 
     def run_step():
         if graphs:
@@ -404,7 +417,7 @@ def main() -> None:
                 graphs[m].replay()
             else:
                 for wt in weights:
-                    wt.run(x_dev[m], out=y_dev[m], stream=stream)
+                    gemm(wt, m)
             b.record(stream)
             torch.cuda.synchronize()
             k_ms.extend([(m, a.elapsed_time(b) / copies)] * copies)
@@ -447,6 +460,7 @@ def main() -> None:
     peak, peak_kind = peaks()
     clocks = sampler.summary()
 
+    torch.cuda.synchronize()
     graphs.clear()
     for wt in weights:
         wt.close()

@@ -452,6 +452,6 @@ int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t l
     a.yf = yf;
     a.ldy = ldy;
     a.m = m;
-    return dispatch(a, stream);
+    return dispatch(a, stream, w);
 }
 }  // namespace qmm

@@ -71,6 +71,7 @@ template <> struct Cfg<kNVFP4> {
 struct TcParams {
     const uint8_t* __restrict__ scales_tiled;  // [row_blocks][kchunks][128][SB]
     uint16_t* __restrict__ y;
+    float* __restrict__ yf;                    // when set: fp32 output (row-parallel partials)
     float* __restrict__ partial;               // [grid][2][128][8]
     unsigned int* __restrict__ counters;       // [row_blocks]
     int64_t ldy;
@@ -344,7 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
-                        if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                        if (row < p.n && col < p.m) {
+                            if (p.yf) p.yf[(int64_t)col * p.ldy + row] = acc[i];
+                            else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                        }
                     }
                 }
                 named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
@@ -405,7 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 for (int e = 0; e < 2; ++e) {
                     const int idx = t + 512 * e, rl = idx >> 3, col = idx & 7;
                     const int row = rb * kRows + rl;
-                    if (row < p.n && col < p.m) p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v[e]);
+                    if (row < p.n && col < p.m) {
+                        if (p.yf) p.yf[(int64_t)col * p.ldy + row] = v[e];
+                        else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v[e]);
+                    }
                 }
             }
             named_sync(1, kConsumers * 32);       // s_red / s_last are reused by the next flush
@@ -646,7 +653,7 @@ void gemv_tc_release(qmm_weight* w) {
 int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, bool* handled) {
     *handled = false;
     const GemvTcState* st = w->tc;
-    if (!st || a.yf || a.m < 1 || a.m > kXRows) return QMM_OK;
+    if (!st || a.m < 1 || a.m > kXRows) return QMM_OK;
     const auto xa = reinterpret_cast<uintptr_t>(a.x);
     if ((xa & 15) || ((a.ldx * 2) & 15)) return QMM_OK;
     const int fmt = a.fmt;
@@ -662,6 +669,7 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     TcParams p;
     p.scales_tiled = st->scales_tiled;
     p.y = a.y;
+    p.yf = a.yf;
     p.partial = st->partial;
     p.counters = st->counters;
     p.ldy = a.ldy;
@@ -810,6 +818,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     TcParams p;
     p.scales_tiled = base;
     p.y = a.y;
+    p.yf = nullptr;
     p.partial = reinterpret_cast<float*>(base + partial_off);
     p.counters = counters;
     p.ldy = a.ldy;

@@ -1,0 +1,87 @@
+"""Tensor parallelism on 2 GPUs (one process per GPU): K-sharded row-parallel
+GEMM with the fp32 NCCL all-reduce, and N-sharded column-parallel shards
+(no collective), both checked against the CPU oracle.  Skipped with fewer
+than 2 GPUs.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _case(mode, n, k, m, seed):
+    import oracle
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+    codes, scales = oracle.quantize(w, mode)
+    x = oracle.f32_to_bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+    return codes, scales, x
+
+
+def _rank(rank, world, uid, mode, n, k, m, q):
+    try:
+        for p in (os.path.join(ROOT, "mlx-runner_b200"), os.path.join(ROOT, "oracle")):
+            sys.path.insert(0, p)
+        import torch
+        import qmm
+        torch.cuda.set_device(rank)
+        codes, scales, x = _case(mode, n, k, m, seed=9)
+        xt = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16)
+        # Row-parallel: this rank's K slice, fp32 partials, one all-reduce.
+        comm = qmm.TPComm(uid, world, rank, m * n)
+        wk = qmm.QuantizedWeight(codes, scales, mode, shard=(1, rank, world))
+        c0 = rank * (k // world)
+        xs = xt[:, c0:c0 + k // world].contiguous().cuda()
+        y_k = comm.run_rowparallel(wk, xs)
+        # Column-parallel: this rank's rows, no collective.
+        wn = qmm.QuantizedWeight(codes, scales, mode, shard=(0, rank, world))
+        y_n = wn.run(xt.cuda())
+        torch.cuda.synchronize()
+        qmm.device_status()
+        q.put((rank, y_k.cpu().view(torch.int16).numpy().view(np.uint16),
+               y_n.cpu().view(torch.int16).numpy().view(np.uint16)))
+        wk.close()
+        wn.close()
+        comm.close()
+    except Exception as exc:
+        q.put((rank, repr(exc), None))
+
+
+@pytest.mark.parametrize("mode,n,k,m", [("nvfp4", 1024, 4096, 3), ("mxfp8", 768, 2048, 1)])
+def test_tp_two_gpus(mode, n, k, m):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import oracle
+    import qmm
+    world = 2
+    uid = qmm.TPComm.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, mode, n, k, m, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        rank, a, b = q.get(timeout=300)
+        out[rank] = (a, b)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, (a, _) in out.items():
+        assert not isinstance(a, str), f"rank {rank}: {a}"
+
+    codes, scales, x = _case(mode, n, k, m, seed=9)
+    ref = oracle.qmm_f64(x, codes, scales, mode)
+    absref = oracle.abs_qmm_f64(x, codes, scales, mode)
+    for rank in range(world):
+        y = oracle.bf16_bits_to_f32(out[rank][0])
+        assert oracle.parity_violations(y, ref, absref) == 0
+    y_n = np.concatenate([oracle.bf16_bits_to_f32(out[r][1]) for r in range(world)], axis=1)
+    assert oracle.parity_violations(y_n, ref, absref) == 0
