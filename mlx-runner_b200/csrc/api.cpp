@@ -441,6 +441,31 @@ extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dt
 
 // Used by tp.cpp: the row-parallel partial product in fp32.
 namespace qmm {
+// Row-parallel decode with the cross-rank sum fused into the decode kernel.
+// *handled = false (every rank alike: the test depends only on shapes and the
+// weight's decode state) when the fused kernel does not apply; x must then
+// still meet its alignment on every rank, else this rank reports an error
+// (its peers' waits time out and report QMM_ERR_TIMEOUT).
+int run_rowparallel_fused(const qmm_weight* w, const TpExchange* ex, const void* x_dev, int64_t m, int64_t ldx,
+                          void* y_dev, int64_t ldy, cudaStream_t stream, bool* handled) {
+    *handled = false;
+    if (!w || !w->tc || m < 1 || m > 8 || m * w->n > ex->cap) return QMM_OK;
+    if (int rc = check_xy(x_dev, m, w->k, ldx, y_dev, w->n, ldy)) return rc;
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || ((ldx * 2) & 15))
+        return set_error(QMM_ERR_BAD_ARGUMENT, "row-parallel decode needs 16-byte aligned x rows");
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(y_dev);
+    a.ldy = ldy;
+    a.m = m;
+    a.tp = ex;
+    if (int rc = launch_gemv_tc(w, a, stream, handled)) return rc;
+    if (!*handled) return set_error(QMM_ERR_CUDA, "row-parallel decode kernel declined a prepared weight");
+    return QMM_OK;
+}
+
 int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, float* yf, int64_t ldy,
                     cudaStream_t stream) {
     if (int rc = check_xy(x_dev, m, w ? w->k : 0, ldx, yf, w ? w->n : 0, ldy)) return rc;

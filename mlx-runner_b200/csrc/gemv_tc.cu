@@ -77,6 +77,13 @@ struct TcParams {
     int64_t ldy;
     int m, n, k;
     int kchunks, row_blocks, units;
+    // Row-parallel exchange (tp_n > 1): final row-block sums go to every
+    // rank's receive slot over NVLink and are added there in rank order.
+    int tp_n, tp_rank, tp_max_rb;
+    int64_t tp_cap;
+    float* tp_recv[kMaxTpRanks];
+    unsigned int* tp_flags[kMaxTpRanks];
+    unsigned int* tp_gen;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -166,6 +173,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     uint64_t* empty = bars + 2 * kStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kStages);
     volatile int* s_last = abort_flag + 1;
+    volatile unsigned int* s_epoch = reinterpret_cast<volatile unsigned int*>(abort_flag + 2);
+    // Row-parallel: row blocks this CTA pushed, finished after its last unit
+    // ([0] = count, then (row block, epoch) pairs).
+    volatile int* s_tp_list = abort_flag + 4;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int u0 = (int)(((int64_t)p.units * blockIdx.x) / gridDim.x);
@@ -179,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             mbar_init(&empty[s], kConsumers);
         }
         *abort_flag = 0;
+        s_tp_list[0] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -328,6 +340,105 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             return fits32 ? (int)(((unsigned)(u + 1) * G - 1u) / (unsigned)p.units)
                           : (int)(((int64_t)(u + 1) * G - 1) / p.units);
         };
+        // Row-parallel exchange of row block rb (final fp32 sums in s_red,
+        // [128 rows][8 columns]).  tp_push writes them to this rank's slot of
+        // every rank's receive buffer and one thread releases them with a
+        // flag per rank (the barrier orders every thread's stores before it);
+        // the CTA then carries on with its units.  After its last unit,
+        // tp_complete waits - for at most kTimeoutNs - until every rank's
+        // flag for each pushed block carries its epoch, and sums the block
+        // over ranks in rank order into y.  Epochs count per row block on the
+        // device, so graph replays stay in step; two receive parities let a
+        // rank run one call ahead of the others.
+        constexpr int kTpList = 16;
+        auto tp_push = [&](int rb) {
+            const int t = threadIdx.x - kFirstConsumer * 32;
+            const int P = p.tp_n, me = p.tp_rank;
+            if (t == 0) *s_epoch = p.tp_gen[rb] + 1u;
+            named_sync(1, kConsumers * 32);
+            const unsigned int epoch = *s_epoch;
+            const int64_t par = epoch & 1u;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int idx = t + 512 * e, col = idx & 7, row = rb * kRows + (idx >> 3);
+                if (row < p.n && col < p.m) {
+                    const float v = s_red[idx];
+                    const int64_t off = (par * P + me) * p.tp_cap + (int64_t)col * p.n + row;
+#pragma unroll
+                    for (int r = 0; r < kMaxTpRanks; ++r)
+                        if (r < P) p.tp_recv[r][off] = v;
+                }
+            }
+            named_sync(1, kConsumers * 32);
+            if (t == 0) {
+                asm volatile("fence.acq_rel.sys;" ::: "memory");
+#pragma unroll
+                for (int r = 0; r < kMaxTpRanks; ++r)
+                    if (r < P)
+                        asm volatile("st.release.sys.global.u32 [%0], %1;"
+                                     ::"l"(p.tp_flags[r] + me * p.tp_max_rb + rb), "r"(epoch) : "memory");
+                p.tp_gen[rb] = epoch;
+                const int n_list = s_tp_list[0];
+                s_tp_list[1 + 2 * n_list] = rb;
+                s_tp_list[2 + 2 * n_list] = (int)epoch;
+                s_tp_list[0] = n_list + 1;
+            }
+            named_sync(1, kConsumers * 32);       // s_red / s_epoch / the list are reused
+        };
+        auto tp_complete = [&]() {
+            const int t = threadIdx.x - kFirstConsumer * 32;
+            const int P = p.tp_n, me = p.tp_rank;
+            const int n_list = s_tp_list[0];
+            if (t == 0) {
+                const uint64_t t0 = gtimer();
+                bool timed_out = false;
+                for (int q = 0; q < n_list && !timed_out; ++q) {
+                    const int rb = s_tp_list[1 + 2 * q];
+                    const unsigned int epoch = (unsigned int)s_tp_list[2 + 2 * q];
+                    for (int src = 0; src < P && !timed_out; ++src) {
+                        for (;;) {
+                            unsigned int f;
+                            asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+                                         : "=r"(f) : "l"(p.tp_flags[me] + src * p.tp_max_rb + rb) : "memory");
+                            if (f == epoch) break;
+                            if (gtimer() - t0 > kTimeoutNs) {
+                                atomicOr(&g_gemv_tc_error, 2u);
+                                timed_out = true;
+                                break;
+                            }
+                        }
+                    }
+                }
+            }
+            named_sync(1, kConsumers * 32);
+            for (int q = 0; q < n_list; ++q) {
+                const int rb = s_tp_list[1 + 2 * q];
+                const int64_t par = (unsigned int)s_tp_list[2 + 2 * q] & 1u;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int idx = t + 512 * e, col = idx & 7, row = rb * kRows + (idx >> 3);
+                    if (row < p.n && col < p.m) {
+                        float v = 0.f;
+                        for (int src = 0; src < P; ++src)
+                            v += __ldcg(p.tp_recv[me] + (par * P + src) * p.tp_cap + (int64_t)col * p.n + row);
+                        p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v);
+                    }
+                }
+            }
+        };
+        // A row block finished inside a flush: push it, or - when the list is
+        // full - push and complete it at once (all threads see the same count).
+        auto tp_finish = [&](int rb) {
+            if (s_tp_list[0] < kTpList) {
+                tp_push(rb);
+            } else {
+                tp_complete();
+                named_sync(1, kConsumers * 32);
+                if (threadIdx.x == kFirstConsumer * 32) s_tp_list[0] = 0;
+                named_sync(1, kConsumers * 32);
+                tp_push(rb);
+            }
+        };
         auto flush = [&](int rb, bool complete) {
             // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
             // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
@@ -339,6 +450,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if (kh == 0) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
+            }
+            if (complete && p.tp_n > 1) {
+                // Each kh = 0 thread rewrites the s_red entries it just read.
+                if (kh == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+                }
+                named_sync(1, kConsumers * 32);
+                tp_finish(rb);
+                return;
             }
             if (complete) {
                 if (kh == 0) {
@@ -405,17 +526,26 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         v[1] += ld[q][1];
                     }
                 }
+                if (p.tp_n > 1) {
+                    // s_red is free here (its last reader was the kh add above).
+                    s_red[t] = v[0];
+                    s_red[t + 512] = v[1];
+                } else {
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int idx = t + 512 * e, rl = idx >> 3, col = idx & 7;
-                    const int row = rb * kRows + rl;
-                    if (row < p.n && col < p.m) {
-                        if (p.yf) p.yf[(int64_t)col * p.ldy + row] = v[e];
-                        else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v[e]);
+                    for (int e = 0; e < 2; ++e) {
+                        const int idx = t + 512 * e, rl = idx >> 3, col = idx & 7;
+                        const int row = rb * kRows + rl;
+                        if (row < p.n && col < p.m) {
+                            if (p.yf) p.yf[(int64_t)col * p.ldy + row] = v[e];
+                            else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v[e]);
+                        }
                     }
                 }
             }
             named_sync(1, kConsumers * 32);       // s_red / s_last are reused by the next flush
+            if (p.tp_n > 1 && *s_last) {
+                tp_finish(rb);
+            }
         };
         for (int i = 0; i < nunits; ++i) {
             const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
@@ -526,6 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 flush(rb, complete);
             }
         }
+        if (p.tp_n > 1) tp_complete();
     }
     __syncthreads();
 }
@@ -670,6 +801,19 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     p.scales_tiled = st->scales_tiled;
     p.y = a.y;
     p.yf = a.yf;
+    p.tp_n = 0;
+    if (a.tp && a.tp->nranks > 1) {
+        p.tp_n = a.tp->nranks;
+        p.tp_rank = a.tp->rank;
+        p.tp_max_rb = a.tp->max_rb;
+        p.tp_cap = a.tp->cap;
+        for (int r = 0; r < kMaxTpRanks; ++r) {
+            p.tp_recv[r] = a.tp->recv[r];
+            p.tp_flags[r] = a.tp->flags[r];
+        }
+        p.tp_gen = a.tp->gen;
+        p.yf = nullptr;
+    }
     p.partial = st->partial;
     p.counters = st->counters;
     p.ldy = a.ldy;
@@ -819,6 +963,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.scales_tiled = base;
     p.y = a.y;
     p.yf = nullptr;
+    p.tp_n = 0;
     p.partial = reinterpret_cast<float*>(base + partial_off);
     p.counters = counters;
     p.ldy = a.ldy;

@@ -42,6 +42,18 @@ struct DeviceInfo {
 int device_info(int device, DeviceInfo* out);
 
 // ---- kernels -----------------------------------------------------------------
+// Peer-memory exchange of a row-parallel (K-sharded) decode: every rank's
+// final fp32 row-block sums go straight into every rank's receive buffer over
+// NVLink and are added there in rank order (gemv_tc.cu).
+constexpr int kMaxTpRanks = 8;
+struct TpExchange {
+    int nranks = 0, rank = 0, max_rb = 0;
+    int64_t cap = 0;                           // floats per (parity, source) receive slot
+    float* recv[kMaxTpRanks] = {};             // rank r's receive buffer [2][nranks][cap]
+    unsigned int* flags[kMaxTpRanks] = {};     // rank r's flags [nranks][max_rb] (epochs)
+    unsigned int* gen = nullptr;               // this rank's per-row-block epoch counters [max_rb]
+};
+
 // Operands of one y = x . dequant(W)^T call, all device pointers.
 struct QmmArgs {
     int fmt;                 // Format
@@ -54,6 +66,7 @@ struct QmmArgs {
     uint16_t* y;             // bf16 [m][ldy]
     int64_t ldy;             // elements
     float* yf = nullptr;     // when set: fp32 output [m][ldy] instead of y
+    const TpExchange* tp = nullptr;  // when set: row-parallel shard summed across ranks into y
     int64_t m, n, k;
 };
 

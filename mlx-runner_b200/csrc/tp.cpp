@@ -1,4 +1,4 @@
-// tp.cpp - tensor-parallel plumbing: NCCL communicator + row-parallel run.
+// tp.cpp - tensor-parallel plumbing: communicator + row-parallel run.
 //
 // The reference has no distributed backend (--tp is parsed and logged as a
 // single-device stub, src/main.zig:210-215, :338-340); the sharding here is
@@ -9,6 +9,15 @@
 // as on one GPU (adding bf16-rounded partials in bf16 measurably exceeds a
 // 2e-3 relative error at 2+ ranks).
 //
+// For decode shapes (M <= 8, resident weight with decode-kernel state) the
+// reduction is fused into the decode kernel: each rank's final fp32 row-block
+// sums go over NVLink straight into every rank's receive buffer (CUDA IPC
+// mappings exchanged at communicator creation) and are added in rank order -
+// one launch, no NCCL call, no separate conversion.  Every rank takes the same
+// path: the choice depends only on the communicator (agreed by all ranks at
+// creation) and on shapes.  Otherwise: fp32 partials, one NCCL fp32
+// all-reduce, one rounding to bf16.  QMM_TP_FUSED=0 disables the fused path.
+//
 // NCCL is loaded with dlopen on first use (the copy already in the process,
 // e.g. torch's, if any; else $QMM_NCCL_LIBRARY; else libnccl.so.2), so the
 // library itself loads on machines without NCCL.
@@ -17,6 +26,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include <nccl.h>
 
@@ -27,6 +37,8 @@ int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t l
                     cudaStream_t stream);
 int launch_f32_to_bf16(const float* in, int64_t rows, int64_t cols, int64_t ld_in, uint16_t* out, int64_t ld_out,
                        cudaStream_t stream);
+int run_rowparallel_fused(const qmm_weight* w, const TpExchange* ex, const void* x_dev, int64_t m, int64_t ldx,
+                          void* y_dev, int64_t ldy, cudaStream_t stream, bool* handled);
 }  // namespace qmm
 
 struct qmm_comm {
@@ -34,6 +46,9 @@ struct qmm_comm {
     int nranks = 0, rank = 0, device = -1;
     float* partial = nullptr;   // fp32 [capacity] partial sums
     int64_t capacity = 0;
+    // Fused row-parallel exchange (peer receive buffers mapped over CUDA IPC).
+    bool fused = false;
+    qmm::TpExchange ex;
 };
 
 namespace {
@@ -44,6 +59,7 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     bool ok = false;
 };
@@ -62,9 +78,10 @@ void load_nccl() {
     g_api.CommInitRank = reinterpret_cast<decltype(g_api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
     g_api.CommDestroy = reinterpret_cast<decltype(g_api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
     g_api.AllReduce = reinterpret_cast<decltype(g_api.AllReduce)>(dlsym(h, "ncclAllReduce"));
+    g_api.AllGather = reinterpret_cast<decltype(g_api.AllGather)>(dlsym(h, "ncclAllGather"));
     g_api.GetErrorString = reinterpret_cast<decltype(g_api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
     g_api.ok = g_api.GetUniqueId && g_api.CommInitRank && g_api.CommDestroy && g_api.AllReduce &&
-               g_api.GetErrorString;
+               g_api.AllGather && g_api.GetErrorString;
 }
 
 int nccl(int* rc_out) {
@@ -78,6 +95,100 @@ int nccl(int* rc_out) {
 
 int nccl_fail(ncclResult_t r, const char* what) {
     return qmm::set_error(QMM_ERR_NCCL, "%s: %s", what, g_api.GetErrorString ? g_api.GetErrorString(r) : "?");
+}
+
+// Frees the fused-exchange resources of c (peer mappings, local buffers).
+void release_fused(qmm_comm* c) {
+    for (int r = 0; r < c->nranks && r < qmm::kMaxTpRanks; ++r) {
+        if (r == c->rank) continue;
+        if (c->ex.recv[r]) cudaIpcCloseMemHandle(c->ex.recv[r]);
+        if (c->ex.flags[r]) cudaIpcCloseMemHandle(c->ex.flags[r]);
+    }
+    if (c->rank < qmm::kMaxTpRanks) {
+        cudaFree(c->ex.recv[c->rank]);
+        cudaFree(c->ex.flags[c->rank]);
+    }
+    cudaFree(c->ex.gen);
+    c->ex = qmm::TpExchange();
+    c->fused = false;
+}
+
+// Collective (every rank calls it in the same order): allocates this rank's
+// receive buffer and flags, exchanges CUDA IPC handles with ncclAllGather,
+// maps the peers' buffers, and agrees (ncclAllReduce min) on whether every
+// rank succeeded.  Returns an error only for NCCL failures; a CUDA failure on
+// any rank leaves every rank on the NCCL path.
+int setup_fused(qmm_comm* c, int64_t cap) {
+    const int P = c->nranks, me = c->rank;
+    const char* env = std::getenv("QMM_TP_FUSED");
+    if (P < 2 || P > qmm::kMaxTpRanks || cap <= 0 || (env && env[0] == '0')) return QMM_OK;
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return QMM_OK;
+    const int max_rb = (int)((cap + 127) / 128);
+    int ok = 1;
+    float* recv = nullptr;
+    unsigned int* flags = nullptr;
+    unsigned int* gen = nullptr;
+    ok = ok && cudaMalloc(&recv, (size_t)2 * P * cap * sizeof(float)) == cudaSuccess;
+    ok = ok && cudaMalloc(&flags, (size_t)P * max_rb * sizeof(unsigned int)) == cudaSuccess;
+    ok = ok && cudaMalloc(&gen, (size_t)max_rb * sizeof(unsigned int)) == cudaSuccess;
+    ok = ok && cudaMemset(flags, 0, (size_t)P * max_rb * sizeof(unsigned int)) == cudaSuccess;
+    ok = ok && cudaMemset(gen, 0, (size_t)max_rb * sizeof(unsigned int)) == cudaSuccess;
+    cudaIpcMemHandle_t mine[2];
+    std::memset(mine, 0, sizeof(mine));
+    ok = ok && cudaIpcGetMemHandle(&mine[0], recv) == cudaSuccess;
+    ok = ok && cudaIpcGetMemHandle(&mine[1], flags) == cudaSuccess;
+    // Exchange [P][2 handles] and the success flags.
+    const size_t hb = sizeof(mine);
+    uint8_t* dbuf = nullptr;
+    int* dok = nullptr;
+    int rc = QMM_OK;
+    if (cudaMalloc(&dbuf, hb * (P + 1)) != cudaSuccess || cudaMalloc(&dok, sizeof(int)) != cudaSuccess) {
+        ok = 0;  // still take part in the collectives below
+    }
+    std::vector<uint8_t> all(hb * P);
+    if (dbuf && dok) {
+        cudaMemcpy(dbuf + hb * P, mine, hb, cudaMemcpyHostToDevice);
+        cudaMemcpy(dok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+        if (ncclResult_t r = g_api.AllGather(dbuf + hb * P, dbuf, hb, ncclUint8, c->comm, s)) rc = nccl_fail(r, "ncclAllGather");
+        else if (ncclResult_t r2 = g_api.AllReduce(dok, dok, 1, ncclInt32, ncclMin, c->comm, s)) rc = nccl_fail(r2, "ncclAllReduce");
+        cudaStreamSynchronize(s);
+        cudaMemcpy(all.data(), dbuf, hb * P, cudaMemcpyDeviceToHost);
+        cudaMemcpy(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost);
+    }
+    c->ex.nranks = P;
+    c->ex.rank = me;
+    c->ex.max_rb = max_rb;
+    c->ex.cap = cap;
+    c->ex.recv[me] = recv;
+    c->ex.flags[me] = flags;
+    c->ex.gen = gen;
+    int opened = ok;
+    if (ok && rc == QMM_OK) {
+        for (int r = 0; r < P; ++r) {
+            if (r == me) continue;
+            cudaIpcMemHandle_t h[2];
+            std::memcpy(h, all.data() + hb * r, hb);
+            void* pr = nullptr;
+            void* pf = nullptr;
+            opened = opened && cudaIpcOpenMemHandle(&pr, h[0], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            if (pr) c->ex.recv[r] = static_cast<float*>(pr);
+            opened = opened && cudaIpcOpenMemHandle(&pf, h[1], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            if (pf) c->ex.flags[r] = static_cast<unsigned int*>(pf);
+        }
+        // Every rank must have mapped every peer.
+        cudaMemcpy(dok, &opened, sizeof(int), cudaMemcpyHostToDevice);
+        if (ncclResult_t r = g_api.AllReduce(dok, dok, 1, ncclInt32, ncclMin, c->comm, s)) rc = nccl_fail(r, "ncclAllReduce");
+        cudaStreamSynchronize(s);
+        cudaMemcpy(&opened, dok, sizeof(int), cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dbuf);
+    cudaFree(dok);
+    cudaStreamDestroy(s);
+    cudaGetLastError();   // a failed IPC call leaves a sticky-free error; it is handled by `ok`
+    c->fused = ok && opened && rc == QMM_OK;
+    if (!c->fused) release_fused(c);
+    return rc;
 }
 
 }  // namespace
@@ -126,6 +237,12 @@ extern "C" int qmm_tp_comm_create(const void* id128, int nranks, int rank, int64
         delete c;
         return nccl_fail(r, "ncclCommInitRank");
     }
+    if (int frc = setup_fused(c, max_partial_elems)) {
+        g_api.CommDestroy(c->comm);
+        cudaFree(c->partial);
+        delete c;
+        return frc;
+    }
     *out = c;
     return QMM_OK;
 }
@@ -136,6 +253,7 @@ extern "C" int qmm_tp_comm_destroy(qmm_comm* c) {
     if (c->comm && g_api.ok) {
         if (ncclResult_t r = g_api.CommDestroy(c->comm)) rc = nccl_fail(r, "ncclCommDestroy");
     }
+    release_fused(c);
     if (c->partial) cudaFree(c->partial);
     delete c;
     return rc;
@@ -164,6 +282,11 @@ extern "C" int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const vo
     if (ldy < n) return set_error(QMM_ERR_BAD_SHAPE, "ldy < n");
     if (m == 0 || n == 0) return QMM_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (c->fused) {
+        bool handled = false;
+        if (int rc = qmm::run_rowparallel_fused(w, &c->ex, x_dev, m, ldx, y_dev, ldy, s, &handled)) return rc;
+        if (handled) return QMM_OK;
+    }
     if (int rc = qmm::run_partial_f32(w, x_dev, m, ldx, c->partial, n, s)) return rc;
     if (ncclResult_t r = g_api.AllReduce(c->partial, c->partial, (size_t)(m * n), ncclFloat32, ncclSum, c->comm, s))
         return nccl_fail(r, "ncclAllReduce(f32)");
