@@ -52,7 +52,7 @@ constexpr int kStages = 4;
 constexpr int kBox = kRows * 128;          // one 2D TMA box: 128 rows x 128 code bytes
 constexpr int kCodeBytes = 2 * kBox;       // 32 KB: 256 code bytes per row per unit
 constexpr int kXRows = 8;                  // x rows staged per unit (M padded to 8)
-constexpr int kConverters = 4;             // x-converter warps (tokens m = v, v + 4)
+constexpr int kConverters = 3;             // x-converter warps (tokens m = v, v + 3, v + 6)
 constexpr int kConsumers = 16;             // 8 row groups x 2 k halves
 constexpr int kFirstConsumer = 1 + kConverters;  // warp index of consumer 0
 constexpr int kThreads = (1 + kConverters + kConsumers) * 32;  // producer, converters, consumers
@@ -151,7 +151,18 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-template <int FMT>
+// x layout of the B fragments (nvfp4; mxfp8 always uses kXlTokens):
+//   kXlTokens   column n of an mma = x row n; the group scale multiplies the
+//               weight fragment (f16) before the mma.  Any M <= 8.
+//   kXlGroups2  column n = 2 q + t: group slot q (the quad lane whose codes
+//               the k rows hold) x x row t.  The block-diagonal x makes each
+//               accumulator column one group's partial sum, scaled after the
+//               mma in fp32.  M <= 2.
+//               (A two-mma form for M <= 4, n = 4 q + t, measured slower
+//               than kXlTokens at M = 3, 4.)
+constexpr int kXlTokens = 0, kXlGroups2 = 1;
+
+template <int FMT, int XL>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
                                                                    const __grid_constant__ CUtensorMap xmap,
                                                                    TcParams p) {
@@ -168,10 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     float* s_xs = reinterpret_cast<float*>(s_xf + kStages * kXfBytes);  // kStages x 8
     float* s_red = s_xs + kStages * 8;                                  // 128 x 8 (k-half sums)
     uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + kRows * 8);
-    uint64_t* full = bars;
-    uint64_t* xready = bars + kStages;
-    uint64_t* empty = bars + 2 * kStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kStages);
+    uint64_t* full = bars;                  // weight tiles (codes + scales) landed
+    uint64_t* xready = bars + kStages;      // f16 x fragments written
+    uint64_t* empty = bars + 2 * kStages;   // every consumer is done with the stage
+    uint64_t* xfull = bars + 3 * kStages;   // raw x chunk landed
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 4 * kStages);
     volatile int* s_last = abort_flag + 1;
     volatile unsigned int* s_epoch = reinterpret_cast<volatile unsigned int*>(abort_flag + 2);
     // Row-parallel: row blocks this CTA pushed, finished after its last unit
@@ -186,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&xfull[s], 1);
             mbar_init(&xready[s], kConverters);
             mbar_init(&empty[s], kConsumers);
         }
@@ -200,19 +213,22 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            // Weight bytes of a unit (codes + scales) and its x chunk.
+            // Weight bytes of a unit (codes + scales) and, on a barrier of its
+            // own, its x chunk: M rows of 256-element boxes (an L2 hit after
+            // the first CTA), converted while the weights are still in flight.
             auto issue_w = [&](int i) {
                 const int s = i % kStages, u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
-                mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes + kXRawBytes);
+                mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes);
                 tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 256, rb * kRows);
                 tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], kc * 256 + 128, rb * kRows);
                 bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)u * kScaleBytes, kScaleBytes, &full[s]);
             };
             auto issue_x = [&](int i) {
                 const int s = i % kStages, kc = (u0 + i) % p.kchunks;
+                mbar_expect_tx(&xfull[s], (uint32_t)(KC / 256) * (uint32_t)p.m * 512u);
 #pragma unroll
                 for (int xb = 0; xb < KC / 256; ++xb)   // x rows of the chunk, 256 elements per box
-                    tma_2d(s_xraw + s * kXRawBytes + xb * kXRows * 512, &xmap, &full[s], kc * KC + 256 * xb, 0);
+                    tma_2d(s_xraw + s * kXRawBytes + xb * p.m * 512, &xmap, &xfull[s], kc * KC + 256 * xb, 0);
             };
             // The first ring of weight tiles streams before the wait on the
             // previous grid (programmatic dependent launch): only x (and the
@@ -235,11 +251,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 const uint64_t t0 = gtimer();
                 while (!mbar_try(&full[i % kStages], (uint32_t)(i / kStages) & 1u) && gtimer() - t0 < kTimeoutNs) {
                 }
+                while (!mbar_try(&xfull[i % kStages], (uint32_t)(i / kStages) & 1u) && gtimer() - t0 < kTimeoutNs) {
+                }
             }
         }
     } else if (warp < kFirstConsumer) {
         // ---------------- x converters ----------------
-        // Warp cv converts x rows m = cv, cv + 4 (m < M).  B-fragment slots of x
+        // Warp cv converts x rows m = cv, cv + 3, cv + 6 (m < M).  B-fragment slots of x
         // rows >= M are zero for the whole launch and their x-scale factors 1
         // (their accumulator columns are never stored).
         const int cv = warp - 1, ct = threadIdx.x - 32;
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         for (int i = 0; i < nunits; ++i) {
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)(i / kStages) & 1u;
-            if (!mbar_wait(&full[s], ph, abort_flag)) break;
+            if (!mbar_wait(&xfull[s], ph, abort_flag)) break;
             const uint16_t* raw = reinterpret_cast<const uint16_t*>(s_xraw + s * kXRawBytes);
             float* xs = s_xs + s * 8;
             // Lane L owns x elements [E L, E L + E) of every row of the chunk
@@ -258,12 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             // 2^-e into [2^14, 2^15), converted to f16 and stored into the
             // B-fragment slot that element run belongs to.  Slots of rows
             // m >= M stay zero (cleared once before the first unit).
-            // The raw chunk arrives as 256-element TMA boxes: element (m, k)
-            // sits at box k / 256, row m, column k % 256.
+            // The raw chunk arrives as 256-element TMA boxes of M rows:
+            // element (m, k) sits at box k / 256, row m, column k % 256.
             constexpr int E = KC / 32;             // 16 (nvfp4) or 8 (mxfp8)
             uint8_t* xf = s_xf + s * kXfBytes;
             const int k0 = E * lane;
-            const uint16_t* rbase = raw + (k0 >> 8) * (kXRows * 256) + (k0 & 255);
+            const uint16_t* rbase = raw + (k0 >> 8) * (p.m * 256) + (k0 & 255);
             for (int m = cv; m < p.m; m += kConverters) {
                 float v[E];
                 uint32_t w[E / 2];
@@ -298,11 +316,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 }
                 if constexpr (FMT == kNVFP4) {
                     // run R = k / 8 of 8 elements -> super-step su = R / 16,
-                    // quad c = (R / 4) % 4, step pair jp = 4 su + R % 4.
+                    // quad c = (R / 4) % 4, step pair jp = 4 su + R % 4.  The
+                    // B-fragment lane is 4 n + c for the run's mma column n.
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const int R = 2 * lane + q, jp = 4 * (R >> 4) + (R & 3), c = (R >> 2) & 3;
-                        *reinterpret_cast<uint4*>(xf + (jp * 32 + 4 * m + c) * 16) =
+                        int bl;
+                        if constexpr (XL == kXlTokens) bl = 4 * m + c;              // n = m
+                        else bl = 9 * c + 4 * m;                                     // n = 2 c + m
+                        *reinterpret_cast<uint4*>(xf + (jp * 32 + bl) * 16) =
                             make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
                     }
                 } else {
@@ -440,6 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             }
         };
         auto flush = [&](int rb, bool complete) {
+            if constexpr (XL == kXlGroups2) {
+                // Lanes c of a quad hold x rows 0, 1 over group slot c: add the
+                // slots (fixed butterfly order); lane c = 0 then holds columns 0, 1.
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
+                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
+                    if (c != 0) acc[i] = 0.f;
+                }
+            }
             // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
             // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
             if (kh == 1) {
@@ -547,6 +579,57 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 tp_finish(rb);
             }
         };
+        // nvfp4 unit with group-slot x columns (kXlGroups2): the codes enter
+        // the mma unscaled (E2M1 -> f16 is exact); each half super-step (jp
+        // 0-1: the chunk's first 16 codes, jp 2-3: the last 16) fills
+        // accumulators whose column 2c + t is group slot c of x row t, which
+        // the group scales of rows r0 / r1 then weight in fp32.
+        auto consume_groups = [&](const uint8_t* cs, const uint8_t* ss, const uint8_t* xf, float xs0, float xs1) {
+            float u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int si = 0; si < 2; ++si) {
+                const int su = kh + 2 * si;
+                const uint8_t* cb = cs + (su >> 1) * kBox;
+                const int ch = (4 * su + c) & 7;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0 * 128 + ((ch ^ (r0 & 7)) << 4));
+                const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1 * 128 + ((ch ^ (r1 & 7)) << 4));
+                // Scales of group slot c (its two halves) for rows r0 and r1.
+                const float2 sa0 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c)));
+                const float2 sa1 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c)));
+                uint32_t h0[16], h1[16];
+                e2m1x8_to_f16x2(w0.x, *reinterpret_cast<uint32_t(*)[4]>(&h0[0]));
+                e2m1x8_to_f16x2(w0.y, *reinterpret_cast<uint32_t(*)[4]>(&h0[4]));
+                e2m1x8_to_f16x2(w0.z, *reinterpret_cast<uint32_t(*)[4]>(&h0[8]));
+                e2m1x8_to_f16x2(w0.w, *reinterpret_cast<uint32_t(*)[4]>(&h0[12]));
+                e2m1x8_to_f16x2(w1.x, *reinterpret_cast<uint32_t(*)[4]>(&h1[0]));
+                e2m1x8_to_f16x2(w1.y, *reinterpret_cast<uint32_t(*)[4]>(&h1[4]));
+                e2m1x8_to_f16x2(w1.z, *reinterpret_cast<uint32_t(*)[4]>(&h1[8]));
+                e2m1x8_to_f16x2(w1.w, *reinterpret_cast<uint32_t(*)[4]>(&h1[12]));
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int jq = 0; jq < 2; ++jq) {
+                        const int jp = 2 * half + jq;
+                        const uint32_t a0[4] = {h0[4 * jp], h1[4 * jp], h0[4 * jp + 1], h1[4 * jp + 1]};
+                        const uint32_t a1[4] = {h0[4 * jp + 2], h1[4 * jp + 2], h0[4 * jp + 3], h1[4 * jp + 3]};
+                        // da / db: two chains over the step pair's two mmas.
+                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        mma16816(da, a0, bx.x, bx.y);
+                        mma16816(db, a1, bx.z, bx.w);
+                    }
+                    const float fa0 = half ? sa0.y : sa0.x, fa1 = half ? sa1.y : sa1.x;
+                    u[0] = fmaf(da[0] + db[0], fa0, u[0]);
+                    u[1] = fmaf(da[1] + db[1], fa0, u[1]);
+                    u[2] = fmaf(da[2] + db[2], fa1, u[2]);
+                    u[3] = fmaf(da[3] + db[3], fa1, u[3]);
+                }
+            }
+            acc[0] = fmaf(u[0], xs0, acc[0]);
+            acc[1] = fmaf(u[1], xs1, acc[1]);
+            acc[2] = fmaf(u[2], xs0, acc[2]);
+            acc[3] = fmaf(u[3], xs1, acc[3]);
+        };
         for (int i = 0; i < nunits; ++i) {
             const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
             if (rb != cur_rb) {
@@ -561,14 +644,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             // A wait that gives up leaves the unit uncomputed but keeps the
             // warp in step with the others (the named barriers in flush must
             // match); the device error word tells the host the output is void.
-            const bool live = mbar_wait(&xready[s], ph, abort_flag);
+            const bool live = mbar_wait(&full[s], ph, abort_flag) && mbar_wait(&xready[s], ph, abort_flag);
             if (live) {
             const uint8_t* cs = s_codes + s * kCodeBytes;
             const uint8_t* ss = s_scales + s * kScaleBytes;
             const uint8_t* xf = s_xf + s * kXfBytes;
             const float* xs = s_xs + s * 8;
-            const float xs0 = xs[2 * c], xs1 = xs[2 * c + 1];
-            if constexpr (FMT == kNVFP4) {
+            // x rows of this lane's accumulator columns.
+            const int t0 = XL == kXlTokens ? 2 * c : 0;
+            const float xs0 = xs[t0], xs1 = xs[t0 + 1];
+            if constexpr (FMT == kNVFP4 && XL != kXlTokens) {
+                consume_groups(cs, ss, xf, xs0, xs1);
+            } else if constexpr (FMT == kNVFP4) {
                 // Two accumulators (even / odd steps) keep two mma chains in flight.
                 float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -695,7 +782,43 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 template <int FMT>
 constexpr int smem_bytes() {
     return 1024 + kStages * (kCodeBytes + kRows * Cfg<FMT>::SB + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
-           kRows * 8 * 4 + 256;
+           kRows * 8 * 4 + 512;
+}
+
+using GemvTcKernel = void (*)(CUtensorMap, CUtensorMap, TcParams);
+
+// Kernel for a format and M, with its dynamic shared memory configured once
+// per device.  nvfp4 takes the group-slot x layout for M <= 2 (the scale
+// leaves the per-code path); QMM_XL=0 keeps the token layout (for A/B runs).
+int pick_kernel(int fmt, int64_t m, int dev, GemvTcKernel* fn, int* smem) {
+    static const bool tokens_only = [] {
+        const char* e = getenv("QMM_XL");
+        return e && e[0] == '0';
+    }();
+    int slot;
+    if (fmt == kMXFP8) {
+        slot = 0;
+        *fn = qmm_gemv_tc_kernel<kMXFP8, kXlTokens>;
+        *smem = smem_bytes<kMXFP8>();
+    } else {
+        *smem = smem_bytes<kNVFP4>();
+        if (!tokens_only && m <= 2) {
+            slot = 1;
+            *fn = qmm_gemv_tc_kernel<kNVFP4, kXlGroups2>;
+        } else {
+            slot = 2;
+            *fn = qmm_gemv_tc_kernel<kNVFP4, kXlTokens>;
+        }
+    }
+    static std::mutex mu;
+    static bool configured[3][64] = {};
+    if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[slot][dev]) {
+        QMM_CUDA_TRY(cudaFuncSetAttribute(*fn, cudaFuncAttributeMaxDynamicSharedMemorySize, *smem));
+        configured[slot][dev] = true;
+    }
+    return QMM_OK;
 }
 
 }  // namespace
@@ -791,7 +914,7 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     CUtensorMap xmap;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
     const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
-    const cuuint32_t box[2] = {256u, (cuuint32_t)kXRows};
+    const cuuint32_t box[2] = {256u, (cuuint32_t)a.m};   // M rows: no zero-filled rows in shared memory
     const cuuint32_t es[2] = {1, 1};
     if (encoder()(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -823,8 +946,6 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     p.kchunks = st->kchunks;
     p.row_blocks = st->row_blocks;
     p.units = st->kchunks * st->row_blocks;
-    static bool configured[2][64] = {};
-    int dev = w->device;
     // Programmatic dependent launch: the kernel may start while the previous
     // kernel on the stream finishes; it streams its first weight tiles, then
     // waits (griddepcontrol.wait) before reading x or writing anything.
@@ -842,23 +963,11 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (fmt == kMXFP8) {
-        if (dev < 64 && !configured[0][dev]) {
-            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kMXFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem_bytes<kMXFP8>()));
-            configured[0][dev] = true;
-        }
-        cfg.dynamicSmemBytes = smem_bytes<kMXFP8>();
-        QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_gemv_tc_kernel<kMXFP8>, st->cmap, xmap, p));
-    } else {
-        if (dev < 64 && !configured[1][dev]) {
-            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kNVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem_bytes<kNVFP4>()));
-            configured[1][dev] = true;
-        }
-        cfg.dynamicSmemBytes = smem_bytes<kNVFP4>();
-        QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_gemv_tc_kernel<kNVFP4>, st->cmap, xmap, p));
-    }
+    GemvTcKernel fn = nullptr;
+    int smem = 0;
+    if (int rc = pick_kernel(fmt, a.m, w->device, &fn, &smem)) return rc;
+    cfg.dynamicSmemBytes = smem;
+    QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, st->cmap, xmap, p));
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;
     return QMM_OK;
@@ -942,7 +1051,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     {
         const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
         const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
-        const cuuint32_t box[2] = {256u, (cuuint32_t)kXRows};
+        const cuuint32_t box[2] = {256u, (cuuint32_t)a.m};
         const cuuint32_t es[2] = {1, 1};
         if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -973,22 +1082,10 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.kchunks = (int)kchunks;
     p.row_blocks = (int)row_blocks;
     p.units = (int)units;
-    static bool configured[2][64] = {};
-    if (fmt == kMXFP8) {
-        if (!configured[0][dev]) {
-            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kMXFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem_bytes<kMXFP8>()));
-            configured[0][dev] = true;
-        }
-        qmm_gemv_tc_kernel<kMXFP8><<<(unsigned)grid, kThreads, smem_bytes<kMXFP8>(), stream>>>(cmap, xmap, p);
-    } else {
-        if (!configured[1][dev]) {
-            QMM_CUDA_TRY(cudaFuncSetAttribute(qmm_gemv_tc_kernel<kNVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem_bytes<kNVFP4>()));
-            configured[1][dev] = true;
-        }
-        qmm_gemv_tc_kernel<kNVFP4><<<(unsigned)grid, kThreads, smem_bytes<kNVFP4>(), stream>>>(cmap, xmap, p);
-    }
+    GemvTcKernel fn = nullptr;
+    int smem = 0;
+    if (int rc = pick_kernel(fmt, a.m, dev, &fn, &smem)) return rc;
+    fn<<<(unsigned)grid, kThreads, smem, stream>>>(cmap, xmap, p);
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;
     return QMM_OK;

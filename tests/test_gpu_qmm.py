@@ -188,6 +188,19 @@ def test_nan_scale_and_nan_code_propagate(cuda_device):
     y = qmm.QuantizedWeight(codes, scales, "mxfp8")(x).float().cpu().numpy()
     assert np.isnan(y[0, 1]) and np.isnan(y[0, 2])
     assert np.isfinite(y[0, 0]) and np.isfinite(y[0, 3])
+    # nvfp4: a UE4M3 NaN scale (0x7F) voids its row for every x row, on each
+    # decode layout (M = 1-2, 3-4 and 5-8 take different kernels).
+    codes4, scales4 = make_weight(300, 512, "nvfp4", seed=6)
+    scales4[7, 3] = 0x7F
+    scales4[200, 31] = 0xFF
+    w4 = qmm.QuantizedWeight(codes4, scales4, "nvfp4")
+    for m in (1, 2, 3, 4, 6):
+        x4 = make_x(m, 512, seed=m).to(cuda_device)
+        y4 = w4(x4).float().cpu().numpy()
+        assert np.isnan(y4[:, 7]).all() and np.isnan(y4[:, 200]).all()
+        ok = np.ones(300, bool)
+        ok[[7, 200]] = False
+        assert np.isfinite(y4[:, ok]).all()
 
 
 def test_empty_m_and_errors_keep_device_usable(cuda_device):
