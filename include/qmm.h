@@ -202,6 +202,45 @@ int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void
 int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m,
                int64_t ldx, void* y_dev, int64_t ldy, void* stream);
 
+/* ---- fused gate / up projection with the SwiGLU epilogue ------------------- */
+
+/* src/model.zig:905-915 mlpForwardQ without its last linear: g = x.Wg^T and
+ * u = x.Wu^T (two namedLinearQ calls, model.zig:218-258), silu(g)
+ * (model.zig:405-415: sigmoid, then g times it) and silu(g) * u
+ * (model.zig:451 mul), each a bf16 array in the reference.  One resident
+ * weight holds both tensors: gate and up rows are interleaved in 64-row
+ * blocks (whole packed rows and scale rows, so the quantisation is bit for
+ * bit), and one kernel writes h = silu(g) * u with the same four bf16
+ * roundings.  gate_* and up_* are two [n, k] tensors of one spec (a fused
+ * [2n, k] gate_up tensor passes its halves).  qmm_run and qmm_dequantize
+ * refuse the result; qmm_weight_info reports n. */
+int qmm_swiglu_weight_create(const void* gate_codes, const void* gate_scales,
+                             const void* up_codes, const void* up_scales, int64_t n, int64_t k,
+                             int64_t ldw, int64_t lds, qmm_quant_spec spec, int src_kind,
+                             void* stream, qmm_weight** out);
+
+/* h[M, n] = silu(x.Wg^T) * (x.Wu^T) in bf16.  M <= 8 runs the decode
+ * kernel, M > 8 the tcgen05 GEMM, both with the SwiGLU epilogue; x rows
+ * that are not 16-byte aligned take the unfused kernels with a
+ * stream-ordered scratch of M x 2n bf16. */
+int qmm_swiglu_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* h_dev,
+                   int64_t ldh, void* stream);
+
+/* ---- lm_head with greedy sampling ----------------------------------------- */
+
+/* src/model.zig:1300-1310 logitsOf (the lm_head linear over the last M
+ * hidden rows) followed, per row, by src/sample.zig:162-170 sampleToken at
+ * temp == 0: ids[r] = argmax of the row's bf16 logits (mlx_argmax_axis;
+ * here the lowest index among equal values, NaN above every number) and
+ * logprobs[r] (nullable) = logprobOf (sample.zig:69-79) = logit[id] -
+ * logsumexp(row), the logsumexp computed in fp32 and rounded to bf16 as the
+ * reference's bf16 array is.  M <= 8 (decode, MTP verify).  The decode
+ * kernel does it in its epilogue, so logits_dev may be NULL (no [M, N]
+ * logits are written); when given, it receives them as qmm_run would. */
+int qmm_lm_head_argmax(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx,
+                       int32_t* ids_dev, float* logprobs_dev, void* logits_dev, int64_t ldl,
+                       void* stream);
+
 /* src/mlx.zig:274 mlx_dequantize: out[N, K] in bf16 (out_dtype BF16) or fp32
  * (F32).  Every mxfp8/nvfp4 value is exact in fp32; bf16 is exact unless a
  * value leaves bf16's range. */

@@ -259,10 +259,12 @@ extern "C" int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy, const void
     return dispatch(a, s);
 }
 
-extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t n, int64_t k, int64_t ldw,
-                                 int64_t lds, qmm_quant_spec spec, int src_kind, void* stream,
-                                 qmm_weight** out) {
-    QMM_FAULT_POINT("qmm_weight_create");
+namespace {
+
+// Upload of one packed weight (codes bit for bit into 16-byte rows, scales
+// unchanged); `prepare` adds the decode kernel's per-weight state.
+int create_weight(const void* codes, const void* scales, int64_t n, int64_t k, int64_t ldw, int64_t lds,
+                  qmm_quant_spec spec, int src_kind, void* stream, bool prepare, qmm_weight** out) {
     if (!out) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
     *out = nullptr;
     if (int rc = check_spec(spec)) return rc;
@@ -305,16 +307,81 @@ extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t 
         if ((e = cudaMemcpy2DAsync(w->scales, w->lds, scales, lds, ngroups, n, kind, s)) != cudaSuccess)
             return fail(e, "copy scales");
     }
-    if (int rc = gemv_tc_prepare(w, s)) {
-        cudaFree(w->codes);
-        cudaFree(w->scales);
-        delete w;
-        return rc;
+    if (prepare) {
+        if (int rc = gemv_tc_prepare(w, s)) {
+            cudaFree(w->codes);
+            cudaFree(w->scales);
+            delete w;
+            return rc;
+        }
     }
     if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
         gemv_tc_release(w);
         return fail(e, "cudaStreamSynchronize");
     }
+    *out = w;
+    return QMM_OK;
+}
+
+}  // namespace
+
+extern "C" int qmm_weight_create(const void* codes, const void* scales, int64_t n, int64_t k, int64_t ldw,
+                                 int64_t lds, qmm_quant_spec spec, int src_kind, void* stream,
+                                 qmm_weight** out) {
+    QMM_FAULT_POINT("qmm_weight_create");
+    return create_weight(codes, scales, n, k, ldw, lds, spec, src_kind, stream, true, out);
+}
+
+extern "C" int qmm_swiglu_weight_create(const void* gate_codes, const void* gate_scales, const void* up_codes,
+                                        const void* up_scales, int64_t n, int64_t k, int64_t ldw, int64_t lds,
+                                        qmm_quant_spec spec, int src_kind, void* stream, qmm_weight** out) {
+    QMM_FAULT_POINT("qmm_swiglu_weight_create");
+    if (!out) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (n <= 0) return set_error(QMM_ERR_BAD_SHAPE, "gate/up weight needs n > 0 (got %lld)", (long long)n);
+    qmm_weight *wg = nullptr, *wu = nullptr;
+    if (int rc = create_weight(gate_codes, gate_scales, n, k, ldw, lds, spec, src_kind, stream, false, &wg)) return rc;
+    if (int rc = create_weight(up_codes, up_scales, n, k, ldw, lds, spec, src_kind, stream, false, &wu)) {
+        qmm_weight_destroy(wg);
+        return rc;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t npad = (n + 63) / 64 * 64;
+    qmm_weight* w = new qmm_weight();
+    w->device = wg->device;
+    w->n = 2 * npad;
+    w->k = k;
+    w->spec = spec;
+    w->ldc = wg->ldc;
+    w->lds = wg->lds;
+    w->swiglu_n = n;
+    auto fail = [&](int rc) {
+        cudaFree(w->codes);
+        cudaFree(w->scales);
+        delete w;
+        qmm_weight_destroy(wg);
+        qmm_weight_destroy(wu);
+        return rc;
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&w->codes, (size_t)(w->ldc * w->n))) != cudaSuccess) return fail(cuda_error(e, "cudaMalloc(codes)"));
+    if ((e = cudaMalloc(&w->scales, (size_t)(w->lds * w->n))) != cudaSuccess) return fail(cuda_error(e, "cudaMalloc(scales)"));
+    if (npad != n) {
+        // Padding rows of the last block: zero codes and scales (outputs 0, never stored).
+        if ((e = cudaMemsetAsync(w->codes, 0, (size_t)(w->ldc * w->n), s)) != cudaSuccess)
+            return fail(cuda_error(e, "cudaMemsetAsync(codes)"));
+        if ((e = cudaMemsetAsync(w->scales, 0, (size_t)(w->lds * w->n), s)) != cudaSuccess)
+            return fail(cuda_error(e, "cudaMemsetAsync(scales)"));
+    }
+    if (int rc = launch_interleave_rows(wg->codes, wu->codes, w->ldc, n, npad, w->codes, s)) return fail(rc);
+    if (int rc = launch_interleave_rows(wg->scales, wu->scales, w->lds, n, npad, w->scales, s)) return fail(rc);
+    if (int rc = gemv_tc_prepare(w, s)) return fail(rc);
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
+        gemv_tc_release(w);
+        return fail(cuda_error(e, "cudaStreamSynchronize"));
+    }
+    qmm_weight_destroy(wg);
+    qmm_weight_destroy(wu);
     *out = w;
     return QMM_OK;
 }
@@ -375,7 +442,7 @@ extern "C" int qmm_weight_destroy(qmm_weight* w) {
 
 extern "C" int qmm_weight_info(const qmm_weight* w, int64_t* n, int64_t* k, qmm_quant_spec* spec, int* device) {
     if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
-    if (n) *n = w->n;
+    if (n) *n = w->swiglu_n > 0 ? w->swiglu_n : w->n;
     if (k) *k = w->k;
     if (spec) *spec = w->spec;
     if (device) *device = w->device;
@@ -407,6 +474,7 @@ extern "C" int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_
     QMM_FAULT_POINT("qmm_run");
     if (!transpose) return set_error(QMM_ERR_BAD_ARGUMENT, "only transpose=true (W [N, K]) is supported");
     if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight runs through qmm_swiglu_run");
     if (int rc = check_xy(x_dev, m, w->k, ldx, y_dev, w->n, ldy)) return rc;
     if (m == 0 || w->n == 0) return QMM_OK;
     QmmArgs a;
@@ -417,6 +485,96 @@ extern "C" int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_
     a.ldy = ldy;
     a.m = m;
     return dispatch(a, static_cast<cudaStream_t>(stream), w);
+}
+
+extern "C" int qmm_lm_head_argmax(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx,
+                                  int32_t* ids_dev, float* logprobs_dev, void* logits_dev, int64_t ldl,
+                                  void* stream) {
+    QMM_FAULT_POINT("qmm_lm_head_argmax");
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight has no logits");
+    if (m < 0 || m > gemv_max_m())
+        return set_error(QMM_ERR_BAD_SHAPE, "greedy sampling takes 0..%d rows (m=%lld)", gemv_max_m(), (long long)m);
+    if (m == 0 || w->n == 0) return QMM_OK;
+    if (!ids_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "ids is NULL");
+    if (logits_dev) {
+        if (int rc = check_xy(x_dev, m, w->k, ldx, logits_dev, w->n, ldl)) return rc;
+    } else {
+        // check_xy with a stand-in output: x alone is validated here.
+        if (int rc = check_xy(x_dev, m, w->k, ldx, ids_dev, 1, 1)) return rc;
+    }
+    if (w->n > INT32_MAX) return set_error(QMM_ERR_BAD_SHAPE, "n=%lld exceeds 32-bit indices", (long long)w->n);
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(logits_dev);
+    a.ldy = logits_dev ? ldl : w->n;
+    a.m = m;
+    a.argmax_ids = ids_dev;
+    a.argmax_lp = logprobs_dev;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bool handled = false;
+    if (int rc = launch_gemv_tc(w, a, s, &handled)) return rc;
+    if (handled) return QMM_OK;
+    // Outside the decode kernel's envelope: the logits (the caller's buffer
+    // or stream-ordered scratch), then the sampling kernel.
+    uint16_t* y = static_cast<uint16_t*>(logits_dev);
+    int64_t ldy = ldl;
+    if (!y) {
+        QMM_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&y), (size_t)(m * w->n * 2), s));
+        ldy = w->n;
+    }
+    QmmArgs b = a;
+    b.argmax_ids = nullptr;
+    b.argmax_lp = nullptr;
+    b.y = y;
+    b.ldy = ldy;
+    int rc = dispatch(b, s, w);
+    if (rc == QMM_OK) rc = launch_argmax_rows(y, ldy, m, w->n, ids_dev, logprobs_dev, s);
+    if (!logits_dev) {
+        cudaError_t e = cudaFreeAsync(y, s);
+        if (rc == QMM_OK && e != cudaSuccess) rc = cuda_error(e, "cudaFreeAsync");
+    }
+    return rc;
+}
+
+extern "C" int qmm_swiglu_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* h_dev,
+                              int64_t ldh, void* stream) {
+    QMM_FAULT_POINT("qmm_swiglu_run");
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (w->swiglu_n <= 0) return set_error(QMM_ERR_BAD_ARGUMENT, "not a gate/up weight (qmm_swiglu_weight_create)");
+    if (int rc = check_xy(x_dev, m, w->k, ldx, h_dev, w->swiglu_n, ldh)) return rc;
+    if (m == 0) return QMM_OK;
+    QmmArgs a;
+    if (int rc = weight_args(w, &a)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(h_dev);
+    a.ldy = ldh;
+    a.m = m;
+    a.swiglu_n = w->swiglu_n;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bool handled = false;
+    if (m <= gemv_max_m()) {
+        if (int rc = launch_gemv_tc(w, a, s, &handled)) return rc;
+    } else {
+        if (int rc = launch_gemm(a, s, &handled)) return rc;
+    }
+    if (handled) return QMM_OK;
+    // Outside the fused kernels' envelope (unaligned x): the interleaved
+    // gate / up outputs into stream-ordered scratch, then the SwiGLU step.
+    uint16_t* y = nullptr;
+    QMM_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&y), (size_t)(m * w->n * 2), s));
+    QmmArgs b = a;
+    b.swiglu_n = 0;
+    b.y = y;
+    b.ldy = w->n;
+    int rc = dispatch(b, s, w);
+    if (rc == QMM_OK) rc = launch_swiglu_apply(y, w->n, m, w->swiglu_n, static_cast<uint16_t*>(h_dev), ldh, s);
+    cudaError_t e = cudaFreeAsync(y, s);
+    if (rc == QMM_OK && e != cudaSuccess) rc = cuda_error(e, "cudaFreeAsync");
+    return rc;
 }
 
 extern "C" int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m, int64_t ldx,
@@ -433,6 +591,7 @@ extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dt
         return set_error(QMM_ERR_UNSUPPORTED_DTYPE, "dequantize output dtype %d (BF16 or F32)", out_dtype);
     QmmArgs a;
     if (int rc = weight_args(w, &a)) return rc;
+    if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight has no single dequantized form");
     if (w->n == 0) return QMM_OK;
     if (!out_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
     return launch_dequant(a.fmt, a.codes, a.ldc, a.scales, a.lds, a.n, a.k, out_dev, out_dtype == QMM_DTYPE_BF16,

@@ -89,4 +89,30 @@ __device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
     return r;
 }
 
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// silu(g) * u from the fp32 gate / up sums of two outputs (g0, u0) and
+// (g1, u1), bf16x2 out (low half = first), with the reference's sequence of
+// bf16 arrays (src/model.zig:905-915 mlpForwardQ: g and u are bf16 linear
+// outputs; silu (model.zig:405-415) is sigmoid(g) then g * sigmoid(g), each
+// a bf16 array; then that times u): g, u and sigmoid(g) are rounded to bf16
+// (nearest even), and the two products are bf16 multiplies, which round the
+// exact product once - as fp32 products rounded to bf16 would.  The sigmoid
+// itself is computed in fp32 to about 2 ulp before its bf16 rounding.
+__device__ __forceinline__ uint32_t swiglu_bf16x2(float g0, float g1, float u0, float u1) {
+    const uint32_t gb = f32x2_to_bf16x2(g0, g1), ub = f32x2_to_bf16x2(u0, u1);
+    const float2 g = bf16x2_to_float2(gb);
+    const float s0 = __fdividef(1.0f, 1.0f + __expf(-g.x));
+    const float s1 = __fdividef(1.0f, 1.0f + __expf(-g.y));
+    const uint32_t sb = f32x2_to_bf16x2(s0, s1);
+    uint32_t t, h;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(gb), "r"(sb));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(h) : "r"(t), "r"(ub));
+    return h;
+}
+
+__device__ __forceinline__ uint16_t swiglu_bf16(float g, float u) {
+    return static_cast<uint16_t>(swiglu_bf16x2(g, 0.0f, u, 0.0f) & 0xFFFFu);
+}
+
 }  // namespace qmm

@@ -62,8 +62,11 @@ constexpr int kXHalfBytes = kHalfT * kBK * 2;   // 16 KB
 constexpr int kXBytes = 2 * kXHalfBytes;        // 32 KB
 constexpr int kWBytes = kTileW * kBK * 2;       // 8 KB
 constexpr int kCodeRingBytes = 32768;
+// SwiGLU epilogue: a gate-row warp and its up-row warp swap half of each
+// 32 x 32 fp32 accumulator chunk (rows padded to 17 words), both ways.
+constexpr int kXchBytes = 2 * 2 * 32 * 17 * 4;
 constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + kCodeRingBytes + 1024 /*align*/ +
-                           1024 /*barriers + flags*/;
+                           1024 /*barriers + flags*/ + kXchBytes;
 constexpr int kDequantWarps = 16;
 constexpr int kEpiWarps = 4;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -75,6 +78,9 @@ struct GemmParams {
     int64_t ldc, lds, ldy;
     int m, n, k;
     int kblocks, w_tiles, num_tiles;
+    // > 0: W rows are gate / up interleaved in 64-row blocks and y receives
+    // silu(g) * u, tile rows 0-63 -> y columns [64 tile, 64 tile + 64).
+    int swiglu_n;
 };
 
 // ---- PTX wrappers --------------------------------------------------------------
@@ -285,8 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
     uint64_t* cempty = cfull + kCStages;                      // kCStages
     volatile int* abort_flag = reinterpret_cast<volatile int*>(cempty + kCStages);
     uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(cempty + kCStages) + 1;
-    static_assert(kStages * (kXBytes + kWBytes) + kCodeRingBytes + (3 * kStages + 3 + 2 * 16) * 8 + 8 + 1024 <=
-                  kSmemBytes, "shared-memory carve-up exceeds the allocation");
+    uint64_t* xch_full = cempty + kCStages + 1;               // SwiGLU hand-over: up chunk written
+    uint64_t* xch_empty = xch_full + 1;                       // ... and read
+    float* smem_xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 1024);
+    static_assert((3 * kStages + 3 + 2 * 16 + 1 + 2) * 8 <= 1024, "barrier area");
+    static_assert(kStages * (kXBytes + kWBytes) + kCodeRingBytes + 1024 + kXchBytes + 1024 <= kSmemBytes,
+                  "shared-memory carve-up exceeds the allocation");
     static_assert(kCStages * kCBytes == kCodeRingBytes && kCStages <= 16, "code ring size");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -304,6 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         mbar_init(tmem_full, 1);
         mbar_init(tmem_empty, kEpiWarps);
         mbar_init(drain, 1);
+        mbar_init(xch_full, kEpiWarps);
+        mbar_init(xch_empty, kEpiWarps);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -412,7 +424,17 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue: TMEM -> bf16 -> y ----------------
         const int q = warp & 3;                     // TMEM lanes 32q .. 32q + 31
-        for (int lt = 0; lt < my_tiles; ++lt) {
+        // SwiGLU: gate-row warp q (rows 0-63) and up-row warp q + 2 (rows
+        // 64-127) swap halves of each 32-token chunk through shared memory
+        // - the up warp sends tokens 0-15, the gate warp tokens 16-31 - and
+        // each computes silu(g) * u for its 16 tokens.  Counted hand-overs
+        // on two mbarriers, every wait bounded.
+        const bool up_warp = q >= 2;
+        float* x_out = smem_xch + ((q & 1) * 2 + (up_warp ? 0 : 1)) * 32 * 17;
+        const float* x_in = smem_xch + ((q & 1) * 2 + (up_warp ? 1 : 0)) * 32 * 17;
+        uint32_t xc = 0;
+        bool live = true;
+        for (int lt = 0; lt < my_tiles && live; ++lt) {
             if (!mbar_wait(tmem_full, (uint32_t)lt & 1u, abort_flag)) break;
             tc_fence_after();
             const int t = (int)blockIdx.x + lt * (int)gridDim.x;
@@ -423,6 +445,33 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                 if (tok0 + c * 32 >= p.m) break;        // uniform across the warp
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+                if (p.swiglu_n > 0) {
+                    const int tmax = min(32, p.m - (tok0 + c * 32));
+                    const int j0 = up_warp ? 16 : 0;       // this warp's tokens j0 .. j0 + 15
+                    if (!mbar_wait(xch_empty, (xc & 1u) ^ 1u, abort_flag)) { live = false; break; }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) x_out[lane * 17 + j] = __uint_as_float(up_warp ? r[j] : r[16 + j]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_full);
+                    if (!mbar_wait(xch_full, xc & 1u, abort_flag)) { live = false; break; }
+                    const int64_t hc = (int64_t)(t % p.w_tiles) * 64 + (q & 1) * 32 + lane;
+                    if (hc < p.swiglu_n) {
+                        uint16_t* hp = p.y + (int64_t)(tok0 + c * 32) * p.ldy + hc;
+#pragma unroll
+                        for (int j = 0; j < 16; j += 2) {
+                            const float m0 = __uint_as_float(up_warp ? r[16 + j] : r[j]);
+                            const float m1 = __uint_as_float(up_warp ? r[17 + j] : r[j + 1]);
+                            const float o0 = x_in[lane * 17 + j], o1 = x_in[lane * 17 + j + 1];
+                            const uint32_t hv = up_warp ? swiglu_bf16x2(o0, o1, m0, m1) : swiglu_bf16x2(m0, m1, o0, o1);
+                            if (j0 + j < tmax) hp[(int64_t)(j0 + j) * p.ldy] = (uint16_t)(hv & 0xFFFFu);
+                            if (j0 + j + 1 < tmax) hp[(int64_t)(j0 + j + 1) * p.ldy] = (uint16_t)(hv >> 16);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_empty);
+                    ++xc;
+                    continue;
+                }
                 if (w_row < p.n) {
                     uint16_t* yp = p.y + (int64_t)(tok0 + c * 32) * p.ldy + w_row;
                     const int tmax = min(32, p.m - (tok0 + c * 32));
@@ -570,6 +619,8 @@ int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     p.m = (int)a.m; p.n = (int)a.n; p.k = (int)a.k;
     p.kblocks = (p.k + kBK - 1) / kBK;
     p.w_tiles = (p.n + kTileW - 1) / kTileW;
+    p.swiglu_n = (int)a.swiglu_n;
+    if (a.swiglu_n > 0 && (a.n % kTileW)) return QMM_OK;   // gate / up tiles are whole 64 + 64 blocks
     const int64_t tiles = (int64_t)p.w_tiles * ((p.m + kTileT - 1) / kTileT);
     if (tiles > INT32_MAX) return QMM_OK;
     p.num_tiles = (int)tiles;

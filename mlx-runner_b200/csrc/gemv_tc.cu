@@ -77,6 +77,19 @@ struct TcParams {
     int64_t ldy;
     int m, n, k;
     int kchunks, row_blocks, units;
+    // > 0: gate / up rows interleaved in 64-row blocks; y gets silu(g) * u
+    // for swiglu_n columns (row block rb -> columns [64 rb, 64 rb + 64)).
+    int swiglu_n;
+    // Greedy sampling (am_ids set): per x row the index of the largest bf16
+    // output and (am_lp) its log-probability; y is written only when set.
+    // am_keys [8] and am_done are zero between calls (the last CTA resets
+    // them); am_part [row_blocks][8][2] holds (max, sum exp(y - max)) of
+    // each 64-row half block.
+    int32_t* am_ids;
+    float* am_lp;
+    unsigned long long* am_keys;
+    float2* am_part;
+    unsigned int* am_done;
     // Row-parallel exchange (tp_n > 1): final row-block sums go to every
     // rank's receive slot over NVLink and are added there in rank order.
     int tp_n, tp_rank, tp_max_rb;
@@ -146,6 +159,23 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Order-preserving 64-bit key of (value, index): larger values rank higher,
+// NaN above +inf, and among equal values the lower index.
+__device__ __forceinline__ unsigned long long rank_key(float v, uint32_t idx) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t ord = (v != v) ? 0xFFFFFFFFu : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - idx);
+}
+
+// (M, S) <- the log-sum-exp merge of (M, S) and (m, s), S counted at M.
+__device__ __forceinline__ void lse_merge(float& M, float& S, float m, float s) {
+    if (m == -INFINITY) return;
+    if (M == -INFINITY) { M = m; S = s; return; }
+    const float mx = fmaxf(M, m);
+    S = S * expf(M - mx) + s * expf(m - mx);
+    M = mx;
+}
+
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
@@ -162,7 +192,12 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
 //               than kXlTokens at M = 3, 4.)
 constexpr int kXlTokens = 0, kXlGroups2 = 1;
 
-template <int FMT, int XL>
+// Epilogue of a finished row block: y (or the row-parallel exchange), the
+// SwiGLU pair, or greedy sampling.  One kernel instantiation each keeps the
+// plain decode kernel free of the others' registers.
+constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiArgmax = 2;
+
+template <int FMT, int XL, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
                                                                    const __grid_constant__ CUtensorMap xmap,
                                                                    TcParams p) {
@@ -461,6 +496,94 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 tp_push(rb);
             }
         };
+        // Gate / up row block rb, final sums in s_red [128 rows][8 columns]:
+        // rows 0-63 are gate rows 64 rb + r, rows 64-127 their up rows.
+        auto swiglu_out = [&](int rb) {
+            const int t = threadIdx.x - kFirstConsumer * 32;
+            const int r = t & 63, col = t >> 6;
+            const int64_t hc = (int64_t)rb * 64 + r;
+            if (col < p.m && hc < p.swiglu_n)
+                p.y[(int64_t)col * p.ldy + hc] = swiglu_bf16(s_red[r * 8 + col], s_red[(r + 64) * 8 + col]);
+        };
+        // Greedy-sampling epilogue of row block rb (final sums in s_red): the
+        // bf16 outputs (to y when set), one rank key per x row into am_keys,
+        // and (max, sum exp) of each 64-row half into am_part.  Threads
+        // 64 col .. 64 col + 63 take x row col: two warps, rows r, r + 64.
+        auto argmax_out = [&](int rb) {
+            const int t = threadIdx.x - kFirstConsumer * 32;
+            const int col = t >> 6, half = (t >> 5) & 1;
+            unsigned long long key = 0;
+            float l[2], mx = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int rl = half * 32 + lane + 64 * e;   // rows 0-31 / 32-63 (+64)
+                const int row = rb * kRows + rl;
+                const bool ok = row < p.n && col < p.m;
+                const uint16_t b = f32_to_bf16(s_red[rl * 8 + col]);
+                if (ok && p.y) p.y[(int64_t)col * p.ldy + row] = b;
+                l[e] = ok ? bf16_to_f32(b) : -INFINITY;
+                if (ok) key = max(key, rank_key(l[e], (uint32_t)row));
+                mx = fmaxf(mx, l[e]);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                key = max(key, __shfl_xor_sync(0xFFFFFFFFu, key, o));
+                mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+            }
+            float sum = mx == -INFINITY ? 0.0f : expf(l[0] - mx) + expf(l[1] - mx);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+            if (lane == 0 && col < p.m) {
+                if (key) atomicMax(&p.am_keys[col], key);
+                p.am_part[((int64_t)rb * 8 + col) * 2 + half] = make_float2(mx, sum);
+            }
+        };
+        // After this CTA's last flush: the last CTA of the grid to get here
+        // (acq_rel count; each CTA's writes are ordered before its count by
+        // the barrier) merges the half-block (max, sum) pairs of each x row
+        // in a fixed order, writes the id and log-probability and resets the
+        // keys and the count for the next call.
+        auto argmax_finish = [&]() {
+            const int t = threadIdx.x - kFirstConsumer * 32;
+            named_sync(1, kConsumers * 32);
+            if (t == 0) {
+                unsigned prev;
+                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.am_done) : "memory");
+                const int last = prev == gridDim.x - 1 ? 1 : 0;
+                if (last) *p.am_done = 0u;
+                *s_last = last;
+            }
+            named_sync(1, kConsumers * 32);
+            if (!*s_last) return;
+            const int col = t >> 6, j = t & 63;
+            float M = -INFINITY, S = 0.0f;
+            if (col < p.m)
+                for (int i = j; i < 2 * p.row_blocks; i += 64) {
+                    const float2 ps = __ldcg(&p.am_part[((int64_t)(i >> 1) * 8 + col) * 2 + (i & 1)]);
+                    lse_merge(M, S, ps.x, ps.y);
+                }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float m2 = __shfl_xor_sync(0xFFFFFFFFu, M, o), s2 = __shfl_xor_sync(0xFFFFFFFFu, S, o);
+                lse_merge(M, S, m2, s2);
+            }
+            if (lane == 0) {
+                s_red[(col * 2 + (j >> 5)) * 2] = M;
+                s_red[(col * 2 + (j >> 5)) * 2 + 1] = S;
+            }
+            named_sync(1, kConsumers * 32);
+            if (j == 0 && col < p.m) {
+                lse_merge(M, S, s_red[(col * 2 + 1) * 2], s_red[(col * 2 + 1) * 2 + 1]);
+                const unsigned long long key = __ldcg(&p.am_keys[col]);
+                p.am_keys[col] = 0ull;
+                const uint32_t ord = (uint32_t)(key >> 32);
+                const uint32_t idx = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
+                const float lid = ord == 0xFFFFFFFFu ? __uint_as_float(0x7FC00000u)
+                                  : __uint_as_float((ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord);
+                p.am_ids[col] = (int32_t)idx;
+                if (p.am_lp) p.am_lp[col] = lid - bf16_to_f32(f32_to_bf16(M + logf(S)));
+            }
+        };
         auto flush = [&](int rb, bool complete) {
             if constexpr (XL == kXlGroups2) {
                 // Lanes c of a quad hold x rows 0, 1 over group slot c: add the
@@ -483,13 +606,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
             }
-            if (complete && p.tp_n > 1) {
+            const bool to_smem = EPI != kEpiPlain || p.tp_n > 1;
+            if (complete && to_smem) {
                 // Each kh = 0 thread rewrites the s_red entries it just read.
                 if (kh == 0) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
                 }
                 named_sync(1, kConsumers * 32);
+                if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
+                if constexpr (EPI == kEpiArgmax) argmax_out(rb);
+                if constexpr (EPI != kEpiPlain) {
+                    named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
+                    return;
+                }
                 tp_finish(rb);
                 return;
             }
@@ -558,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         v[1] += ld[q][1];
                     }
                 }
-                if (p.tp_n > 1) {
+                if (to_smem) {
                     // s_red is free here (its last reader was the kh add above).
                     s_red[t] = v[0];
                     s_red[t + 512] = v[1];
@@ -575,6 +705,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 }
             }
             named_sync(1, kConsumers * 32);       // s_red / s_last are reused by the next flush
+            if constexpr (EPI != kEpiPlain) {
+                if (*s_last) {
+                    if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
+                    else argmax_out(rb);
+                    named_sync(1, kConsumers * 32);
+                }
+            }
             if (p.tp_n > 1 && *s_last) {
                 tp_finish(rb);
             }
@@ -744,6 +881,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             }
         }
         if (p.tp_n > 1) tp_complete();
+        if constexpr (EPI == kEpiArgmax) argmax_finish();
     }
     __syncthreads();
 }
@@ -790,28 +928,26 @@ using GemvTcKernel = void (*)(CUtensorMap, CUtensorMap, TcParams);
 // Kernel for a format and M, with its dynamic shared memory configured once
 // per device.  nvfp4 takes the group-slot x layout for M <= 2 (the scale
 // leaves the per-code path); QMM_XL=0 keeps the token layout (for A/B runs).
-int pick_kernel(int fmt, int64_t m, int dev, GemvTcKernel* fn, int* smem) {
+int pick_kernel(int fmt, int64_t m, int epi, int dev, GemvTcKernel* fn, int* smem) {
     static const bool tokens_only = [] {
         const char* e = getenv("QMM_XL");
         return e && e[0] == '0';
     }();
-    int slot;
-    if (fmt == kMXFP8) {
-        slot = 0;
-        *fn = qmm_gemv_tc_kernel<kMXFP8, kXlTokens>;
-        *smem = smem_bytes<kMXFP8>();
-    } else {
-        *smem = smem_bytes<kNVFP4>();
-        if (!tokens_only && m <= 2) {
-            slot = 1;
-            *fn = qmm_gemv_tc_kernel<kNVFP4, kXlGroups2>;
-        } else {
-            slot = 2;
-            *fn = qmm_gemv_tc_kernel<kNVFP4, kXlTokens>;
-        }
-    }
+    // One table row per (format / layout) and epilogue.
+    static const GemvTcKernel table[3][3] = {
+        {qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiSwiglu>,
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiArgmax>},
+        {qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiSwiglu>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiArgmax>},
+        {qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiSwiglu>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiArgmax>},
+    };
+    const int row = fmt == kMXFP8 ? 0 : (!tokens_only && m <= 2) ? 1 : 2;
+    *smem = fmt == kMXFP8 ? smem_bytes<kMXFP8>() : smem_bytes<kNVFP4>();
+    *fn = table[row][epi];
+    const int slot = row * 3 + epi;
     static std::mutex mu;
-    static bool configured[3][64] = {};
+    static bool configured[9][64] = {};
     if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!configured[slot][dev]) {
@@ -828,6 +964,10 @@ struct GemvTcState {
     uint8_t* scales_tiled = nullptr;
     float* partial = nullptr;
     unsigned int* counters = nullptr;
+    // Greedy sampling: [8] keys + the CTA count (one allocation), and the
+    // half-block (max, sum exp) pairs [row_blocks][8][2].
+    unsigned long long* am_keys = nullptr;
+    float2* am_part = nullptr;
     int grid = 0, kchunks = 0, row_blocks = 0;
 };
 
@@ -864,6 +1004,8 @@ int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream) {
         cudaFree(st->scales_tiled);
         cudaFree(st->partial);
         cudaFree(st->counters);
+        cudaFree(st->am_keys);
+        cudaFree(st->am_part);
         delete st;
         return cuda_error(e, what);
     };
@@ -875,6 +1017,13 @@ int gemv_tc_prepare(qmm_weight* w, cudaStream_t stream) {
         return fail(e, "cudaMalloc(counters)");
     if ((e = cudaMemsetAsync(st->counters, 0, (size_t)st->row_blocks * sizeof(unsigned int), stream)) != cudaSuccess)
         return fail(e, "cudaMemsetAsync(counters)");
+    // Greedy-sampling state: 8 keys + the CTA count, zero between calls.
+    if ((e = cudaMalloc(&st->am_keys, 9 * sizeof(unsigned long long))) != cudaSuccess)
+        return fail(e, "cudaMalloc(argmax keys)");
+    if ((e = cudaMemsetAsync(st->am_keys, 0, 9 * sizeof(unsigned long long), stream)) != cudaSuccess)
+        return fail(e, "cudaMemsetAsync(argmax keys)");
+    if ((e = cudaMalloc(&st->am_part, (size_t)st->row_blocks * 16 * sizeof(float2))) != cudaSuccess)
+        return fail(e, "cudaMalloc(argmax partials)");
     const int64_t total = (int64_t)tiled;
     const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)info.sms * 8);
     retile_scales_kernel<<<grid, 256, 0, stream>>>(w->scales, w->lds, (int)w->n, (int)(w->k / w->spec.group_size),
@@ -900,6 +1049,8 @@ void gemv_tc_release(qmm_weight* w) {
     cudaFree(w->tc->scales_tiled);
     cudaFree(w->tc->partial);
     cudaFree(w->tc->counters);
+    cudaFree(w->tc->am_keys);
+    cudaFree(w->tc->am_part);
     delete w->tc;
     w->tc = nullptr;
 }
@@ -937,6 +1088,14 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
         p.tp_gen = a.tp->gen;
         p.yf = nullptr;
     }
+    p.swiglu_n = (int)a.swiglu_n;
+    if (a.swiglu_n > 0 && (p.tp_n > 0 || a.yf)) return QMM_OK;   // not combined with the exchange or fp32 output
+    p.am_ids = a.argmax_ids;
+    p.am_lp = a.argmax_lp;
+    p.am_keys = st->am_keys;
+    p.am_part = st->am_part;
+    p.am_done = reinterpret_cast<unsigned int*>(st->am_keys + 8);
+    if (a.argmax_ids && (p.tp_n > 0 || a.yf || a.swiglu_n > 0)) return QMM_OK;
     p.partial = st->partial;
     p.counters = st->counters;
     p.ldy = a.ldy;
@@ -965,7 +1124,8 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     cfg.numAttrs = pdl ? 1 : 0;
     GemvTcKernel fn = nullptr;
     int smem = 0;
-    if (int rc = pick_kernel(fmt, a.m, w->device, &fn, &smem)) return rc;
+    const int epi = a.argmax_ids ? kEpiArgmax : a.swiglu_n > 0 ? kEpiSwiglu : kEpiPlain;
+    if (int rc = pick_kernel(fmt, a.m, epi, w->device, &fn, &smem)) return rc;
     cfg.dynamicSmemBytes = smem;
     QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, st->cmap, xmap, p));
     QMM_CUDA_TRY(cudaGetLastError());
@@ -1073,6 +1233,9 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.y = a.y;
     p.yf = nullptr;
     p.tp_n = 0;
+    p.swiglu_n = 0;
+    p.am_ids = nullptr;
+    p.am_lp = nullptr;
     p.partial = reinterpret_cast<float*>(base + partial_off);
     p.counters = counters;
     p.ldy = a.ldy;
@@ -1084,7 +1247,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.units = (int)units;
     GemvTcKernel fn = nullptr;
     int smem = 0;
-    if (int rc = pick_kernel(fmt, a.m, dev, &fn, &smem)) return rc;
+    if (int rc = pick_kernel(fmt, a.m, kEpiPlain, dev, &fn, &smem)) return rc;
     fn<<<(unsigned)grid, kThreads, smem, stream>>>(cmap, xmap, p);
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;

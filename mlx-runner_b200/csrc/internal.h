@@ -67,8 +67,34 @@ struct QmmArgs {
     int64_t ldy;             // elements
     float* yf = nullptr;     // when set: fp32 output [m][ldy] instead of y
     const TpExchange* tp = nullptr;  // when set: row-parallel shard summed across ranks into y
+    // When > 0: W rows are gate / up interleaved in 64-row blocks (rows
+    // [128 b, 128 b + 64) = gate rows [64 b, 64 b + 64), the next 64 the
+    // matching up rows) and y receives silu(gate) * up, [m][swiglu_n].
+    int64_t swiglu_n = 0;
+    // When set (decode kernel, M <= 8): greedy sampling of each x row -
+    // argmax_ids[m] = the index of the largest bf16 output (lowest index
+    // among equals, NaN above all), argmax_lp[m] (nullable) = that output
+    // minus logsumexp over the row; y (nullable here) still receives the
+    // bf16 outputs when set.
+    int32_t* argmax_ids = nullptr;
+    float* argmax_lp = nullptr;
     int64_t m, n, k;
 };
+
+// Greedy sampling over bf16 rows already in memory (the unfused path):
+// ids[r] / lp[r] for logits [m][ldl] of n columns, one CTA per row.
+int launch_argmax_rows(const uint16_t* logits, int64_t ldl, int64_t m, int64_t n, int32_t* ids, float* lp,
+                       cudaStream_t stream);
+
+// Gate / up interleaving of one packed tensor pair (codes or scales, `pitch`
+// bytes per row, n_half rows each) into dst [2 * npad][pitch]; rows past
+// n_half stay as dst holds them (the caller zeroes them).
+int launch_interleave_rows(const uint8_t* gate, const uint8_t* up, int64_t pitch, int64_t n_half, int64_t npad,
+                           uint8_t* dst, cudaStream_t stream);
+// h[m][n_half] = silu(gate) * up from an interleaved bf16 y [m][ldy] (the
+// unfused path for shapes outside the fused kernels' envelope).
+int launch_swiglu_apply(const uint16_t* y, int64_t ldy, int64_t m, int64_t n_half, uint16_t* h, int64_t ldh,
+                        cudaStream_t stream);
 
 // Split-K GEMV for m <= 8 (decode / MTP verify).  No workspace: the split-K
 // partials are reduced through distributed shared memory inside a cluster.
@@ -114,4 +140,5 @@ struct qmm_weight {
     int64_t ldc = 0;
     uint8_t* scales = nullptr;  // device, row stride lds
     int64_t lds = 0;
+    int64_t swiglu_n = 0;       // > 0: gate / up pair interleaved in 64-row blocks (qmm_swiglu_weight_create)
 };

@@ -273,6 +273,7 @@ extern "C" int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const vo
                                       void* y_dev, int64_t ldy, void* stream) {
     if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_run_rowparallel: injected failure");
     if (!c || !w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight or comm is NULL");
+    if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight is not row-parallel");
     int64_t n = 0, k = 0;
     qmm_weight_info(w, &n, &k, nullptr, nullptr);
     if (m < 0) return set_error(QMM_ERR_BAD_SHAPE, "m < 0");

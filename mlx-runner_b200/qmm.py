@@ -43,6 +43,7 @@ EXPORTS = (
     "qmm_quantized_matmul", "qmm_quantized_matmul_noalloc", "qmm_weight_create", "qmm_weight_create_shard", "qmm_shard_range",
     "qmm_weight_destroy",
     "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
+    "qmm_swiglu_weight_create", "qmm_swiglu_run", "qmm_lm_head_argmax",
     "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
     "qmm_last_error", "qmm_error_pending", "qmm_device_status", "qmm_fault_arm", "qmm_fault_fired",
 )
@@ -110,6 +111,10 @@ def lib() -> ctypes.CDLL:
     L.qmm_run.argtypes = [vp, vp, i64, i64, vp, i64, ctypes.c_bool, vp]
     L.qmm_linear.argtypes = [vp, ctypes.c_bool, vp, i64, i64, vp, i64, vp]
     L.qmm_dequantize.argtypes = [vp, vp, ctypes.c_int32, vp]
+    L.qmm_swiglu_weight_create.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, QuantSpec, i32, vp,
+                                           ctypes.POINTER(vp)]
+    L.qmm_swiglu_run.argtypes = [vp, vp, i64, i64, vp, i64, vp]
+    L.qmm_lm_head_argmax.argtypes = [vp, vp, i64, i64, vp, vp, vp, i64, vp]
     L.qmm_tp_unique_id.argtypes = [vp]
     L.qmm_tp_comm_create.argtypes = [vp, i32, i32, i64, ctypes.POINTER(vp)]
     L.qmm_tp_comm_destroy.argtypes = [vp]
@@ -323,6 +328,22 @@ class QuantizedWeight:
                             _stream_handle(stream)))
         return y.reshape(*x.shape[:-1], self.n) if out is None else y
 
+    def argmax(self, x, logits: bool = False, stream=None):
+        """Greedy sampling of each x row through this (lm_head) weight:
+        (ids int32 [M], logprobs fp32 [M], logits bf16 [M, N] or None)."""
+        torch = _torch()
+        if x.dtype != torch.bfloat16:
+            raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        x2 = _as_2d(x)
+        m = x2.shape[0]
+        ids = torch.empty((m,), dtype=torch.int32, device=x.device)
+        lp = torch.empty((m,), dtype=torch.float32, device=x.device)
+        y = torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device) if logits else None
+        check(lib().qmm_lm_head_argmax(self.handle, x2.data_ptr(), m, x2.stride(0), ids.data_ptr(), lp.data_ptr(),
+                                       y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0,
+                                       _stream_handle(stream)))
+        return ids, lp, y
+
     def dequantize(self, dtype=None, stream=None):
         torch = _torch()
         dtype = dtype or torch.bfloat16
@@ -341,6 +362,42 @@ class QuantizedWeight:
             self.close()
         except Exception:
             pass
+
+
+class SwiGLUWeight(QuantizedWeight):
+    """Gate and up projections of one MLP as a single resident weight whose
+    run() returns h = silu(x.Wg^T) * (x.Wu^T) (src/model.zig:905-915 up to the
+    down projection)."""
+
+    def __init__(self, gate_codes, gate_scales, up_codes, up_scales, mode: str, stream=None):
+        self.spec = make_spec(mode)
+        gc, gs = _src(gate_codes, "U32"), _src(gate_scales, "U8")
+        uc, us = _src(up_codes, "U32"), _src(up_scales, "U8")
+        if gc.kind != uc.kind:
+            raise QmmError(7, "gate and up tensors must both be host or both device arrays")
+        n = int(gate_codes.shape[0])
+        k = int(gate_codes.shape[1]) * 32 // self.spec.bits
+        h = ctypes.c_void_p()
+        check(lib().qmm_swiglu_weight_create(gc.ptr, gs.ptr, uc.ptr, us.ptr, n, k, 0, 0, self.spec, gc.kind,
+                                             _stream_handle(stream), ctypes.byref(h)))
+        self._h = h
+        nn, kk, dev = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        check(lib().qmm_weight_info(h, ctypes.byref(nn), ctypes.byref(kk), None, ctypes.byref(dev)))
+        self.n, self.k, self.device = nn.value, kk.value, dev.value
+
+    def run(self, x, out=None, stream=None):
+        torch = _torch()
+        if x.dtype != torch.bfloat16:
+            raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        x2 = _as_2d(x)
+        m = x2.shape[0]
+        h = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
+        check(lib().qmm_swiglu_run(self.handle, x2.data_ptr(), m, x2.stride(0), h.data_ptr(), h.stride(0),
+                                   _stream_handle(stream)))
+        return h.reshape(*x.shape[:-1], self.n) if out is None else h
+
+    def dequantize(self, dtype=None, stream=None):
+        raise QmmError(7, "a gate/up weight has no single dequantized form")
 
 
 def linear(weight: Optional[QuantizedWeight], x, has_packed_u32: bool = True, out=None, stream=None):

@@ -178,3 +178,86 @@ def rel_frobenius(y: np.ndarray, ref: np.ndarray) -> float:
     ref = np.asarray(ref, dtype=np.float64)
     den = np.linalg.norm(ref)
     return float(np.linalg.norm(y - ref) / (den if den > 0 else 1.0))
+
+
+# ---- SwiGLU (src/model.zig:905-915) -----------------------------------------------
+
+def _f64_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """fp64 -> bf16 bits, one round-to-nearest-even step (no fp32 detour)."""
+    a = np.asarray(a, dtype=np.float64)
+    out = f32_to_bf16_bits(a.astype(np.float32))
+    # Values whose fp32 rounding landed exactly on a bf16 tie would round twice:
+    # redo those from the fp64 value.
+    f32 = a.astype(np.float32).view(np.uint32)
+    tie = (f32 & 0xFFFF) == 0x8000
+    if np.any(tie):
+        lo = (f32[tie] & 0xFFFF0000).view(np.float32).astype(np.float64)
+        hi_bits = ((f32[tie] >> 16) + 1).astype(np.uint16)
+        hi = bf16_bits_to_f32(hi_bits).astype(np.float64)
+        av = a[tie]
+        pick_hi = np.abs(av - hi) < np.abs(av - lo)
+        even = ((f32[tie] >> 16) & 1) == 0
+        eq = np.abs(av - hi) == np.abs(av - lo)
+        pick_hi = pick_hi | (eq & ~even)
+        out[tie] = np.where(pick_hi, hi_bits, (f32[tie] >> 16).astype(np.uint16))
+    return out
+
+
+def swiglu_bf16(g_bits: np.ndarray, u_bits: np.ndarray) -> np.ndarray:
+    """silu(g) * u over bf16 arrays (bits in, bits out) with the reference's
+    sequence of bf16 arrays: sigmoid(g) (model.zig:409), g * sigmoid(g)
+    (:412), that * u (:913, mul :451), each rounded to bf16 (nearest even).
+    The sigmoid is 1 / (1 + e^-g) in fp64 rounded once; the products of two
+    bf16 values are exact in fp64 before their rounding."""
+    g = bf16_bits_to_f32(g_bits).astype(np.float64)
+    u = bf16_bits_to_f32(u_bits).astype(np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        s = 1.0 / (1.0 + np.exp(-g))
+    sb = bf16_bits_to_f32(_f64_to_bf16_bits(s)).astype(np.float64)
+    t = bf16_bits_to_f32(_f64_to_bf16_bits(g * sb)).astype(np.float64)
+    return _f64_to_bf16_bits(t * u)
+
+
+def swiglu_violations(h_bits: np.ndarray, g_ref: np.ndarray, u_ref: np.ndarray, absg: np.ndarray,
+                      absu: np.ndarray, acc_rel: float = 2.0 ** -20) -> int:
+    """Elements of h = silu(g) * u (bf16 bits) outside the exact composition's
+    band: the gate / up sums may each miss by the GEMM bar (1 bf16 ulp +
+    acc_rel * sum|x||w|), carried through silu(g) * u by its derivatives,
+    plus the four bf16 roundings of the chain (2^-8 relative each)."""
+    h = bf16_bits_to_f32(h_bits).astype(np.float64)
+    g, u = np.asarray(g_ref, np.float64), np.asarray(u_ref, np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        sig = 1.0 / (1.0 + np.exp(-g))
+    silu = g * sig
+    dsilu = sig * (1.0 + g * (1.0 - sig))
+    ref = silu * u
+    tg = bf16_ulp(g) + acc_rel * absg
+    tu = bf16_ulp(u) + acc_rel * absu
+    tol = (np.abs(dsilu) * tg * (np.abs(u) + tu) + (np.abs(silu) + np.abs(dsilu) * tg) * tu
+           + 4.0 * 2.0 ** -8 * np.abs(ref) + 2.0 ** -133)
+    bad = ~(np.abs(h - ref) <= tol)
+    both_nan = np.isnan(h) & np.isnan(ref)
+    return int(np.count_nonzero(bad & ~both_nan))
+
+
+# ---- greedy sampling (src/sample.zig:162-170, :69-79) ----------------------------
+
+def greedy_sample(logits_bits: np.ndarray):
+    """Per row of bf16 logits (bits [M, N]): (ids, logprobs).  id = argmax
+    (mlx_argmax_axis; the lowest index among equal values, NaN above every
+    number); logprob = logit[id] - logsumexp(row), the logsumexp in fp64
+    rounded to bf16 (the reference reads a bf16 array back as f32)."""
+    l = bf16_bits_to_f32(np.asarray(logits_bits, dtype=np.uint16)).astype(np.float64)
+    m, n = l.shape
+    ids = np.zeros(m, np.int64)
+    lps = np.zeros(m, np.float64)
+    for r in range(m):
+        row = l[r]
+        nan = np.isnan(row)
+        ids[r] = int(np.argmax(nan)) if nan.any() else int(np.argmax(row))
+        mx = np.nanmax(row) if not nan.all() else np.nan
+        with np.errstate(over="ignore", invalid="ignore"):
+            lse = mx + np.log(np.sum(np.exp(row - mx)))
+        lse_b = bf16_bits_to_f32(_f64_to_bf16_bits(np.array([lse]))).astype(np.float64)[0]
+        lps[r] = row[ids[r]] - lse_b
+    return ids, lps

@@ -128,3 +128,25 @@ def test_bf16_rounding_matches_torch():
     ours = oracle.f32_to_bf16_bits(a)
     theirs = torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(ours, theirs)
+
+
+def test_swiglu_oracle_sequence():
+    """silu(g) * u over bf16 arrays: known values and single RNE rounding."""
+    g = oracle.f32_to_bf16_bits(np.array([0.0, 1.0, -1.0, 10.0, -100.0, 3.5], np.float32))
+    u = oracle.f32_to_bf16_bits(np.array([2.0, 2.0, 2.0, 0.5, 1.0, -1.0], np.float32))
+    h = oracle.bf16_bits_to_f32(oracle.swiglu_bf16(g, u))
+    np.testing.assert_array_equal(h, np.array([0.0, 1.4609375, -0.5390625, 5.0, -0.0, -3.390625], np.float32))
+    a = np.random.default_rng(0).standard_normal(20000) * 3
+    b = oracle._f64_to_bf16_bits(a)
+    cand = np.stack([b - 1, b, b + 1]).astype(np.uint16)
+    best = np.argmin(np.abs(oracle.bf16_bits_to_f32(cand).astype(np.float64) - a), axis=0)
+    assert np.all(best == 1)
+    # The band (about 3% here): the exact composition passes, 6% off does not.
+    gr = np.array([[0.7, -2.0, 4.0]])
+    ur = np.array([[1.5, 0.25, -3.0]])
+    ref = gr / (1 + np.exp(-gr)) * ur
+    hb = oracle.f32_to_bf16_bits(ref.astype(np.float32))
+    zero = np.zeros_like(gr)
+    assert oracle.swiglu_violations(hb, gr, ur, zero, zero) == 0
+    off = oracle.f32_to_bf16_bits((ref * 1.06).astype(np.float32))
+    assert oracle.swiglu_violations(off, gr, ur, zero, zero) == 3
