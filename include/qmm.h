@@ -55,6 +55,12 @@ typedef enum qmm_status {
     QMM_ERR_BAD_MODE = 6,             /* mode string not "mxfp8"/"nvfp4", or group/bits mismatch */
     QMM_ERR_BAD_ARGUMENT = 7,         /* NULL pointer, transpose=false, biases given, bad stride */
     QMM_ERR_MISSING_WEIGHT = 8,       /* ModelError.MissingWeight (model.zig:220, :228) */
+    QMM_ERR_BAD_INDEX_JSON = 10,      /* WeightsError.BadIndexJson      (weights.zig:24) */
+    QMM_ERR_BAD_HEADER = 11,          /* WeightsError.BadHeader         (weights.zig:25) */
+    QMM_ERR_UNSUPPORTED_LAYOUT = 12,  /* WeightsError.UnsupportedLayout (weights.zig:27) */
+    QMM_ERR_MISSING_TENSOR = 13,      /* WeightsError.MissingTensor     (weights.zig:28) */
+    QMM_ERR_DUPLICATE_TENSOR = 14,    /* WeightsError.DuplicateTensor   (weights.zig:29) */
+    QMM_ERR_IO = 15,                  /* a checkpoint file could not be opened or read */
     QMM_ERR_CUDA = 20,                /* a CUDA runtime/driver call failed */
     QMM_ERR_OUT_OF_MEMORY = 21,       /* device allocation failed */
     QMM_ERR_NCCL = 22,                /* an NCCL call failed or NCCL could not be loaded */
@@ -94,6 +100,7 @@ typedef struct qmm_optional_int {
 
 typedef struct qmm_weight qmm_weight;  /* opaque, owns device copies of codes + scales */
 typedef struct qmm_comm qmm_comm;      /* opaque tensor-parallel communicator (NCCL) */
+typedef struct qmm_checkpoint qmm_checkpoint;  /* opaque: an opened sharded safetensors checkpoint */
 
 /* ---- spec inference (pure host; src/weights.zig:132-185) --------------- */
 
@@ -201,6 +208,40 @@ int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void
  * otherwise it forwards to qmm_run. */
 int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* x_dev, int64_t m,
                int64_t ldx, void* y_dev, int64_t ldy, void* stream);
+
+/* ---- checkpoint loading (src/weights.zig:72-121, :241-352) ----------------- */
+
+/* WeightMap.load's reading of a sharded safetensors checkpoint, headers
+ * only: model_dir/model.safetensors.index.json's "weight_map" names the
+ * shards (BadIndexJson otherwise), visited in first-appearance order; per
+ * shard checkShardFile (weights.zig:241-255) reads the u64 LE header length
+ * (0 < n <= 256 MiB, else BadHeader) and parseHeaderJson (:72-121) the
+ * entries: dtype BF16 / F32 / U32 / U8 (else UnsupportedDtype), a shape of
+ * integers (else BadHeader), "conv1d.weight" ending in a unit dimension
+ * (else UnsupportedLayout); here also data_offsets that match the shape and
+ * stay inside the file (else BadHeader).  A name in two shards is
+ * DuplicateTensor.  The checkpoint's spec comes from qmm_infer_quant_spec
+ * over every header.  Names are kept as stored (the reference's name
+ * sanitising is model-specific).  An unreadable file is QMM_ERR_IO. */
+int qmm_checkpoint_open(const char* model_dir, qmm_checkpoint** out);
+int qmm_checkpoint_close(qmm_checkpoint* c);
+/* The inferred spec, and a view of every tensor (valid until close). */
+int qmm_checkpoint_spec(const qmm_checkpoint* c, qmm_quant_spec* spec);
+int qmm_checkpoint_tensors(const qmm_checkpoint* c, const qmm_tensor_info** infos, int64_t* count);
+/* One tensor's bytes, as stored, into dst (QMM_SRC_HOST or QMM_SRC_DEVICE
+ * memory of at least its size); MissingTensor if absent. */
+int qmm_checkpoint_read(const qmm_checkpoint* c, const char* name, void* dst, int64_t dst_bytes,
+                        int dst_kind);
+/* The quantized linear "<prefix>.weight" (U32 codes) + "<prefix>.scales"
+ * (U8) as a resident qmm_weight on the current device (qmm_weight_create:
+ * codes bit for bit, scales re-tiled).  A missing .weight is MissingTensor,
+ * a missing .scales MissingWeight (model.zig:226-228). */
+int qmm_checkpoint_load_linear(const qmm_checkpoint* c, const char* prefix, void* stream,
+                               qmm_weight** out);
+/* A gate / up pair ("<gate_prefix>", "<up_prefix>") as one SwiGLU weight
+ * (qmm_swiglu_weight_create). */
+int qmm_checkpoint_load_swiglu(const qmm_checkpoint* c, const char* gate_prefix,
+                               const char* up_prefix, void* stream, qmm_weight** out);
 
 /* ---- fused gate / up projection with the SwiGLU epilogue ------------------- */
 

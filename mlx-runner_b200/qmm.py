@@ -29,6 +29,8 @@ QMM_OK = 0
 STATUS_NAMES = {
     1: "BadShape", 2: "NonstandardQuant", 3: "InconsistentQuant", 4: "AffineUnsupported",
     5: "UnsupportedDtype", 6: "BadMode", 7: "BadArgument", 8: "MissingWeight",
+    10: "BadIndexJson", 11: "BadHeader", 12: "UnsupportedLayout", 13: "MissingTensor", 14: "DuplicateTensor",
+    15: "IoError",
     20: "CudaError", 21: "OutOfMemory", 22: "NcclError", 23: "Timeout", 24: "NoDevice",
     30: "Injected",
 }
@@ -44,6 +46,8 @@ EXPORTS = (
     "qmm_weight_destroy",
     "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
     "qmm_swiglu_weight_create", "qmm_swiglu_run", "qmm_lm_head_argmax",
+    "qmm_checkpoint_open", "qmm_checkpoint_close", "qmm_checkpoint_spec", "qmm_checkpoint_tensors",
+    "qmm_checkpoint_read", "qmm_checkpoint_load_linear", "qmm_checkpoint_load_swiglu",
     "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
     "qmm_last_error", "qmm_error_pending", "qmm_device_status", "qmm_fault_arm", "qmm_fault_fired",
 )
@@ -115,6 +119,13 @@ def lib() -> ctypes.CDLL:
                                            ctypes.POINTER(vp)]
     L.qmm_swiglu_run.argtypes = [vp, vp, i64, i64, vp, i64, vp]
     L.qmm_lm_head_argmax.argtypes = [vp, vp, i64, i64, vp, vp, vp, i64, vp]
+    L.qmm_checkpoint_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
+    L.qmm_checkpoint_close.argtypes = [vp]
+    L.qmm_checkpoint_spec.argtypes = [vp, ctypes.POINTER(QuantSpec)]
+    L.qmm_checkpoint_tensors.argtypes = [vp, ctypes.POINTER(ctypes.POINTER(TensorInfo)), ctypes.POINTER(i64)]
+    L.qmm_checkpoint_read.argtypes = [vp, ctypes.c_char_p, vp, i64, i32]
+    L.qmm_checkpoint_load_linear.argtypes = [vp, ctypes.c_char_p, vp, ctypes.POINTER(vp)]
+    L.qmm_checkpoint_load_swiglu.argtypes = [vp, ctypes.c_char_p, ctypes.c_char_p, vp, ctypes.POINTER(vp)]
     L.qmm_tp_unique_id.argtypes = [vp]
     L.qmm_tp_comm_create.argtypes = [vp, i32, i32, i64, ctypes.POINTER(vp)]
     L.qmm_tp_comm_destroy.argtypes = [vp]
@@ -411,6 +422,78 @@ def linear(weight: Optional[QuantizedWeight], x, has_packed_u32: bool = True, ou
     check(lib().qmm_linear(weight.handle, has_packed_u32, x2.data_ptr(), x2.shape[0], x2.stride(0),
                            y.data_ptr(), y.stride(0), _stream_handle(stream)))
     return y
+
+
+def _adopt(cls, h: ctypes.c_void_p, spec):
+    obj = cls.__new__(cls)
+    obj.spec = spec
+    obj._h = h
+    n, k, dev = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+    check(lib().qmm_weight_info(h, ctypes.byref(n), ctypes.byref(k), None, ctypes.byref(dev)))
+    obj.n, obj.k, obj.device = n.value, k.value, dev.value
+    return obj
+
+
+class Checkpoint:
+    """A sharded safetensors checkpoint opened from its directory
+    (src/weights.zig WeightMap.load, headers only until a tensor is read)."""
+
+    def __init__(self, model_dir: str):
+        h = ctypes.c_void_p()
+        check(lib().qmm_checkpoint_open(os.fsencode(model_dir), ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def spec(self) -> QuantSpec:
+        s = QuantSpec()
+        check(lib().qmm_checkpoint_spec(self._h, ctypes.byref(s)))
+        return s
+
+    def tensors(self) -> dict:
+        """name -> (dtype name, shape) for every tensor of every shard."""
+        infos = ctypes.POINTER(TensorInfo)()
+        count = ctypes.c_int64()
+        check(lib().qmm_checkpoint_tensors(self._h, ctypes.byref(infos), ctypes.byref(count)))
+        names = {v: k for k, v in DTYPES.items()}
+        out = {}
+        for i in range(count.value):
+            t = infos[i]
+            out[t.name.decode()] = (names[t.dtype], tuple(t.shape[d] for d in range(t.ndim)))
+        return out
+
+    def read(self, name: str):
+        """The tensor's bytes as a numpy array of its dtype and shape."""
+        import numpy as np
+        info = self.tensors().get(name)
+        if info is None:
+            check(lib().qmm_checkpoint_read(self._h, name.encode(), None, 0, SRC_HOST))   # MissingTensor
+        dt, shape = info
+        np_dt = {"BF16": np.uint16, "F32": np.float32, "U32": np.uint32, "U8": np.uint8}[dt]
+        arr = np.empty(shape, dtype=np_dt)
+        check(lib().qmm_checkpoint_read(self._h, name.encode(), arr.ctypes.data, arr.nbytes, SRC_HOST))
+        return arr
+
+    def linear(self, prefix: str, stream=None) -> QuantizedWeight:
+        h = ctypes.c_void_p()
+        check(lib().qmm_checkpoint_load_linear(self._h, prefix.encode(), _stream_handle(stream), ctypes.byref(h)))
+        return _adopt(QuantizedWeight, h, self.spec)
+
+    def swiglu(self, gate_prefix: str, up_prefix: str, stream=None) -> "SwiGLUWeight":
+        h = ctypes.c_void_p()
+        check(lib().qmm_checkpoint_load_swiglu(self._h, gate_prefix.encode(), up_prefix.encode(),
+                                               _stream_handle(stream), ctypes.byref(h)))
+        return _adopt(SwiGLUWeight, h, self.spec)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qmm_checkpoint_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class TPComm:
