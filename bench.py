@@ -220,6 +220,178 @@ def prefill_measure(args, qmm, oracle, dev, world: int, rank: int, barrier, max_
                                  "the block-scaled FP4 peak (~9 PF nominal) needs x quantised to FP4"}}
 
 
+def _rand_nvfp4(n: int, k: int, dev, seed: int):
+    """Packed nvfp4 [n, k] made on the GPU: random codes, finite UE4M3 scales
+    in [2^-7, 2^-3) (timing only; numerics are the tests' job)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    codes = torch.randint(-2**31, 2**31 - 1, (n, k // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
+    scales = torch.randint(0x18, 0x38, (n, k // 16), generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+    return codes, scales
+
+
+def _graph_ms(fn, reps: int) -> float:
+    """Device time per call of fn(stream), captured in a CUDA graph."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(s)
+        fn(s)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms
+
+
+def next_rows_measure(args, qmm, dev) -> dict:
+    """The rows after the headline GEMM, each timed through its C-ABI call in
+    CUDA graphs (inputs larger than L2: weight copies rotate):
+      swiglu_decode   gate/up [17408, 5120] x 2 with the fused epilogue vs the
+                      two GEMVs + torch silu*mul (src/model.zig:905-915)
+      swiglu_prefill  config 3 (x [M, 5120], gate/up 34816 rows) fused vs the
+                      plain gate_up GEMM
+      lm_head_argmax  [248320, 5120] with greedy sampling in the epilogue vs
+                      logits + the sampling kernel (src/sample.zig:162-170)
+      mtp_step_graph  the MTP head's linears + draft and M=3 verify sampling
+                      as one graph vs eager launches"""
+    import torch
+    out = {}
+    peak, peak_kind = peaks()
+    H, FFN, V = 5120, 17408, 248320
+    bpe = 9 / 16          # nvfp4 bytes per weight element (codes + scales)
+    # SwiGLU decode.
+    copies = 3
+    g_u = [(_rand_nvfp4(FFN, H, dev, 10 + i), _rand_nvfp4(FFN, H, dev, 20 + i)) for i in range(copies)]
+    fused = [qmm.SwiGLUWeight(*g, *u, "nvfp4") for g, u in g_u]
+    gates = [qmm.QuantizedWeight(*g, "nvfp4") for g, _ in g_u]
+    ups = [qmm.QuantizedWeight(*u, "nvfp4") for _, u in g_u]
+    del g_u
+    dec = {"workload": "gate/up 2 x [17408, 5120] nvfp4, M = 1..4", "fused_us": {}, "unfused_us": {},
+           "GBs": {}, "frac": {}, "peak": peak, "peak_kind": peak_kind}
+    for m in (1, 2, 3, 4):
+        x = torch.randn((m, H), device=dev).to(torch.bfloat16)
+        h = torch.empty((m, FFN), device=dev, dtype=torch.bfloat16)
+        yg, yu = torch.empty_like(h), torch.empty_like(h)
+
+        def f_fused(st):
+            for w in fused:
+                w.run(x, out=h, stream=st)
+
+        def f_unfused(st):
+            for i in range(copies):
+                gates[i].run(x, out=yg, stream=st)
+                ups[i].run(x, out=yu, stream=st)
+                torch.mul(torch.nn.functional.silu(yg), yu, out=h)
+        t_f = _graph_ms(f_fused, 20) / copies
+        t_u = _graph_ms(f_unfused, 20) / copies
+        gbs = 2 * FFN * H * bpe / (t_f * 1e-3) / 1e9
+        dec["fused_us"][m] = 1e3 * t_f
+        dec["unfused_us"][m] = 1e3 * t_u
+        dec["GBs"][m] = gbs
+        dec["frac"][m] = gbs / peak
+    out["swiglu_decode"] = dec
+    for w in fused + gates + ups:
+        w.close()
+    # SwiGLU prefill at config 3.
+    m = args.prefill_m
+    g, u = _rand_nvfp4(FFN, H, dev, 30), _rand_nvfp4(FFN, H, dev, 31)
+    sw = qmm.SwiGLUWeight(*g, *u, "nvfp4")
+    cat = qmm.QuantizedWeight(torch.cat([g[0], u[0]]), torch.cat([g[1], u[1]]), "nvfp4")
+    del g, u
+    x = torch.randn((m, H), device=dev).to(torch.bfloat16)
+    h = torch.empty((m, FFN), device=dev, dtype=torch.bfloat16)
+    y = torch.empty((m, 2 * FFN), device=dev, dtype=torch.bfloat16)
+    t_f = _graph_ms(lambda st: sw.run(x, out=h, stream=st), 3)
+    t_p = _graph_ms(lambda st: cat.run(x, out=y, stream=st), 3)
+    out["swiglu_prefill"] = {"workload": f"cfg3 x [{m}, 5120] . gate_up [34816, 5120] nvfp4", "fused_ms": t_f,
+                             "plain_ms": t_p, "fused_tflops": 2.0 * m * 2 * FFN * H / (t_f * 1e-3) / 1e12}
+    sw.close()
+    cat.close()
+    del x, h, y
+    # lm_head + greedy sampling.
+    lm = qmm.QuantizedWeight(*_rand_nvfp4(V, H, dev, 40), "nvfp4")
+    am = {"workload": "lm_head [248320, 5120] nvfp4 + argmax + logprob, M = 1, 3", "fused_us": {},
+          "unfused_us": {}, "GBs": {}, "frac": {}, "peak": peak, "peak_kind": peak_kind}
+    for m in (1, 3):
+        x = torch.randn((m, H), device=dev).to(torch.bfloat16)
+        ids = torch.empty((m,), device=dev, dtype=torch.int32)
+        lp = torch.empty((m,), device=dev, dtype=torch.float32)
+        logits = torch.empty((m, V), device=dev, dtype=torch.bfloat16)
+
+        fused_call = lambda st: qmm.check(qmm.lib().qmm_lm_head_argmax(
+            lm.handle, x.data_ptr(), m, H, ids.data_ptr(), lp.data_ptr(), None, 0, st.cuda_stream))
+
+        def unfused_call(st):
+            # logits to HBM through the same decode kernel, then torch's
+            # argmax and logsumexp over them (the reference's op sequence)
+            lm.run(x, out=logits, stream=st)
+            torch.argmax(logits, dim=1)
+            torch.logsumexp(logits.float(), dim=1)
+        t_f = _graph_ms(fused_call, 10)
+        t_u = _graph_ms(unfused_call, 10)
+        gbs = V * H * bpe / (t_f * 1e-3) / 1e9
+        am["fused_us"][m] = 1e3 * t_f
+        am["unfused_us"][m] = 1e3 * t_u
+        am["GBs"][m] = gbs
+        am["frac"][m] = gbs / peak
+    out["lm_head_argmax"] = am
+    # MTP draft step + M=3 verify sampling as one graph.
+    shapes = {"fc": (H, 2 * H), "q": (12288, H), "k": (1024, H), "v": (1024, H), "o": (H, 6144), "down": (H, FFN)}
+    ws = {k: qmm.QuantizedWeight(*_rand_nvfp4(n, kk, dev, 50 + i), "nvfp4") for i, (k, (n, kk)) in enumerate(shapes.items())}
+    ws["mlp"] = qmm.SwiGLUWeight(*_rand_nvfp4(FFN, H, dev, 60), *_rand_nvfp4(FFN, H, dev, 61), "nvfp4")
+    bf = torch.bfloat16
+    b = {"cat": torch.randn((1, 2 * H), device=dev).to(bf), "fused": torch.empty((1, H), device=dev, dtype=bf),
+         "q": torch.empty((1, 12288), device=dev, dtype=bf), "k": torch.empty((1, 1024), device=dev, dtype=bf),
+         "v": torch.empty((1, 1024), device=dev, dtype=bf), "attn": torch.randn((1, 6144), device=dev).to(bf),
+         "o": torch.empty((1, H), device=dev, dtype=bf), "ff": torch.empty((1, FFN), device=dev, dtype=bf),
+         "mp": torch.empty((1, H), device=dev, dtype=bf), "vx": torch.randn((3, H), device=dev).to(bf),
+         "id1": torch.empty((1,), device=dev, dtype=torch.int32), "lp1": torch.empty((1,), device=dev),
+         "id3": torch.empty((3,), device=dev, dtype=torch.int32), "lp3": torch.empty((3,), device=dev)}
+
+    def mtp_step(st):
+        ws["fc"].run(b["cat"], out=b["fused"], stream=st)
+        for k in ("q", "k", "v"):
+            ws[k].run(b["fused"], out=b[k], stream=st)
+        ws["o"].run(b["attn"], out=b["o"], stream=st)
+        ws["mlp"].run(b["o"], out=b["ff"], stream=st)
+        ws["down"].run(b["ff"], out=b["mp"], stream=st)
+        qmm.check(qmm.lib().qmm_lm_head_argmax(lm.handle, b["mp"].data_ptr(), 1, H, b["id1"].data_ptr(),
+                                               b["lp1"].data_ptr(), None, 0, st.cuda_stream))
+        qmm.check(qmm.lib().qmm_lm_head_argmax(lm.handle, b["vx"].data_ptr(), 3, H, b["id3"].data_ptr(),
+                                               b["lp3"].data_ptr(), None, 0, st.cuda_stream))
+    t_g = _graph_ms(mtp_step, 10)
+    st = torch.cuda.current_stream()
+    mtp_step(st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        mtp_step(st)
+    e1.record()
+    torch.cuda.synchronize()
+    t_e = e0.elapsed_time(e1) / 10
+    step_bytes = sum(n * kk for n, kk in shapes.values()) * bpe + 2 * FFN * H * bpe + 2 * V * H * bpe
+    out["mtp_step_graph"] = {"workload": "MTP head linears (fc 10240->5120, q/k/v, o, gate/up SwiGLU, down) + "
+                                         "lm_head sampling M=1 and M=3 verify, nvfp4, 9 launches",
+                             "graph_us": 1e3 * t_g, "eager_us": 1e3 * t_e,
+                             "GBs": step_bytes / (t_g * 1e-3) / 1e9}
+    for w in list(ws.values()) + [lm]:
+        w.close()
+    return out
+
+
 def bf16_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -266,6 +438,7 @@ def main() -> None:
     ap.add_argument("--prefill-m", type=int, default=PREFILL["m"])
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-warmup", type=int, default=2)
+    ap.add_argument("--no-next", action="store_true", help="skip the SwiGLU / lm_head / MTP-graph measurements")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -468,6 +641,9 @@ def main() -> None:
     prefill = None
     if not args.no_prefill:
         prefill = prefill_measure(args, qmm, oracle, dev, world, rank, barrier, max_over_ranks)
+    next_rows = None
+    if not args.no_next and world == 1:
+        next_rows = next_rows_measure(args, qmm, dev)
 
     if rank == 0:
         line = {
@@ -489,6 +665,7 @@ def main() -> None:
             "gpu_launches": args.steps * copies * len(M_SET) * launches_per_gemm,
             "clocks": clocks,
             "prefill": prefill,
+            "next_rows": next_rows,
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
