@@ -581,19 +581,23 @@ def main() -> None:
         ms = max_over_ranks(ev0.elapsed_time(ev1))
 
         # Kernel-alone timing of the dominant kernel (events on its stream):
-        # one pass of `copies` launches per M, averaged per launch.
+        # `passes` back-to-back passes of `copies` launches per M (one graph
+        # replay each), averaged per launch, so the graph launch itself and
+        # the first launch's start are spread over many kernels.
         k_ms = []
+        passes = 10
         for m in M_SET:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            if graphs:
-                graphs[m].replay()
-            else:
-                for wt in weights:
-                    gemm(wt, m)
+            for _ in range(passes):
+                if graphs:
+                    graphs[m].replay()
+                else:
+                    for wt in weights:
+                        gemm(wt, m)
             b.record(stream)
             torch.cuda.synchronize()
-            k_ms.extend([(m, a.elapsed_time(b) / copies)] * copies)
+            k_ms.extend([(m, a.elapsed_time(b) / (passes * copies))] * copies)
 
     # e2e: host buffers through the C ABI, copies inside the timed region.
     x_host = {m: x_full[m][:, rank * k_shard:(rank + 1) * k_shard].contiguous().pin_memory() for m in M_SET}
