@@ -251,19 +251,25 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             // Weight bytes of a unit (codes + scales) and, on a barrier of its
             // own, its x chunk: M rows of 256-element boxes (an L2 hit after
             // the first CTA), converted while the weights are still in flight.
+            // Units are issued in order, so their (row block, chunk) advance by
+            // one step each: no division per unit.
+            int w_rb = u0 / p.kchunks, w_kc = u0 - w_rb * p.kchunks, x_kc = w_kc;
             auto issue_w = [&](int i) {
-                const int s = i % kStages, u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
+                const int s = i % kStages;
                 mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes);
-                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], kc * 256, rb * kRows);
-                tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], kc * 256 + 128, rb * kRows);
-                bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)u * kScaleBytes, kScaleBytes, &full[s]);
+                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], w_kc * 256, w_rb * kRows);
+                tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], w_kc * 256 + 128, w_rb * kRows);
+                bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)(u0 + i) * kScaleBytes, kScaleBytes,
+                        &full[s]);
+                if (++w_kc == p.kchunks) { w_kc = 0; ++w_rb; }
             };
             auto issue_x = [&](int i) {
-                const int s = i % kStages, kc = (u0 + i) % p.kchunks;
+                const int s = i % kStages;
                 mbar_expect_tx(&xfull[s], (uint32_t)(KC / 256) * (uint32_t)p.m * 512u);
 #pragma unroll
                 for (int xb = 0; xb < KC / 256; ++xb)   // x rows of the chunk, 256 elements per box
-                    tma_2d(s_xraw + s * kXRawBytes + xb * p.m * 512, &xmap, &xfull[s], kc * KC + 256 * xb, 0);
+                    tma_2d(s_xraw + s * kXRawBytes + xb * p.m * 512, &xmap, &xfull[s], x_kc * KC + 256 * xb, 0);
+                if (++x_kc == p.kchunks) x_kc = 0;
             };
             // The first ring of weight tiles streams before the wait on the
             // previous grid (programmatic dependent launch): only x (and the
@@ -733,23 +739,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 // Scales of group slot c (its two halves) for rows r0 and r1.
                 const float2 sa0 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c)));
                 const float2 sa1 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c)));
-                uint32_t h0[16], h1[16];
-                e2m1x8_to_f16x2(w0.x, *reinterpret_cast<uint32_t(*)[4]>(&h0[0]));
-                e2m1x8_to_f16x2(w0.y, *reinterpret_cast<uint32_t(*)[4]>(&h0[4]));
-                e2m1x8_to_f16x2(w0.z, *reinterpret_cast<uint32_t(*)[4]>(&h0[8]));
-                e2m1x8_to_f16x2(w0.w, *reinterpret_cast<uint32_t(*)[4]>(&h0[12]));
-                e2m1x8_to_f16x2(w1.x, *reinterpret_cast<uint32_t(*)[4]>(&h1[0]));
-                e2m1x8_to_f16x2(w1.y, *reinterpret_cast<uint32_t(*)[4]>(&h1[4]));
-                e2m1x8_to_f16x2(w1.z, *reinterpret_cast<uint32_t(*)[4]>(&h1[8]));
-                e2m1x8_to_f16x2(w1.w, *reinterpret_cast<uint32_t(*)[4]>(&h1[12]));
+                const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int jq = 0; jq < 2; ++jq) {
                         const int jp = 2 * half + jq;
-                        const uint32_t a0[4] = {h0[4 * jp], h1[4 * jp], h0[4 * jp + 1], h1[4 * jp + 1]};
-                        const uint32_t a1[4] = {h0[4 * jp + 2], h1[4 * jp + 2], h0[4 * jp + 3], h1[4 * jp + 3]};
+                        // Word jp of rows r0 / r1 (8 codes each) widened just
+                        // before its mmas: 8 live f16 pairs instead of 32.
+                        uint32_t ha[4], hb[4];
+                        e2m1x8_to_f16x2(wa[jp], ha);
+                        e2m1x8_to_f16x2(wb[jp], hb);
+                        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
+                        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
                         // da / db: two chains over the step pair's two mmas.
                         const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         mma16816(da, a0, bx.x, bx.y);
@@ -767,8 +770,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             acc[2] = fmaf(u[2], xs0, acc[2]);
             acc[3] = fmaf(u[3], xs1, acc[3]);
         };
+        int next_rb = u0 / p.kchunks, next_kc = u0 - next_rb * p.kchunks;   // advanced per unit
         for (int i = 0; i < nunits; ++i) {
-            const int u = u0 + i, rb = u / p.kchunks, kc = u % p.kchunks;
+            const int rb = next_rb, kc = next_kc;
+            if (++next_kc == p.kchunks) { next_kc = 0; ++next_rb; }
             if (rb != cur_rb) {
                 if (cur_rb >= 0) flush(cur_rb, rb_first_unit == 0);   // a row block ends inside this CTA
                 cur_rb = rb;
