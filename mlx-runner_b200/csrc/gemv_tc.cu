@@ -192,10 +192,11 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
 //               than kXlTokens at M = 3, 4.)
 constexpr int kXlTokens = 0, kXlGroups2 = 1;
 
-// Epilogue of a finished row block: y (or the row-parallel exchange), the
-// SwiGLU pair, or greedy sampling.  One kernel instantiation each keeps the
-// plain decode kernel free of the others' registers.
-constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiArgmax = 2;
+// Epilogue of a finished row block: y (bf16, or fp32 partial sums), the
+// SwiGLU pair, greedy sampling, or the row-parallel exchange over NVLink.
+// One kernel instantiation each keeps the plain decode kernel free of the
+// others' code and registers.
+constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiArgmax = 2, kEpiTp = 3;
 
 template <int FMT, int XL, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
@@ -590,65 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 if (p.am_lp) p.am_lp[col] = lid - bf16_to_f32(f32_to_bf16(M + logf(S)));
             }
         };
-        auto flush = [&](int rb, bool complete) {
-            if constexpr (XL == kXlGroups2) {
-                // Lanes c of a quad hold x rows 0, 1 over group slot c: add the
-                // slots (fixed butterfly order); lane c = 0 then holds columns 0, 1.
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
-                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
-                    if (c != 0) acc[i] = 0.f;
-                }
-            }
-            // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
-            // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
-            if (kh == 1) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
-            }
-            named_sync(1, kConsumers * 32);
-            if (kh == 0) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
-            }
-            const bool to_smem = EPI != kEpiPlain || p.tp_n > 1;
-            if (complete && to_smem) {
-                // Each kh = 0 thread rewrites the s_red entries it just read.
-                if (kh == 0) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
-                }
-                named_sync(1, kConsumers * 32);
-                if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
-                if constexpr (EPI == kEpiArgmax) argmax_out(rb);
-                if constexpr (EPI != kEpiPlain) {
-                    named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
-                    return;
-                }
-                tp_finish(rb);
-                return;
-            }
-            if (complete) {
-                if (kh == 0) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
-                        if (row < p.n && col < p.m) {
-                            if (p.yf) p.yf[(int64_t)col * p.ldy + row] = acc[i];
-                            else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
-                        }
-                    }
-                }
-                named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
-                return;
-            }
-            const int slot = (rb == first_rb) ? 0 : 1;
-            float* part = p.partial + ((int64_t)blockIdx.x * 2 + slot) * kRows * 8;
-            if (kh == 0) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
-            }
+        // Counter step of row block rb after this CTA wrote its partial: the
+        // last contributor to arrive sums every contributor's partial.
+        auto arrive_partial = [&](int rb) {
+            constexpr bool to_smem = EPI != kEpiPlain;
             // The barrier orders the CTA's partial writes before thread 64's
             // gpu-scope fence, which then releases them with the counter
             // update; the last arriver's fence acquires the other CTAs' writes
@@ -711,16 +657,77 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 }
             }
             named_sync(1, kConsumers * 32);       // s_red / s_last are reused by the next flush
-            if constexpr (EPI != kEpiPlain) {
+            if constexpr (EPI == kEpiSwiglu || EPI == kEpiArgmax) {
                 if (*s_last) {
                     if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
                     else argmax_out(rb);
                     named_sync(1, kConsumers * 32);
                 }
             }
-            if (p.tp_n > 1 && *s_last) {
-                tp_finish(rb);
+            if constexpr (EPI == kEpiTp) {
+                if (*s_last) tp_finish(rb);
             }
+        };
+        auto flush = [&](int rb, bool complete) {
+            if constexpr (XL == kXlGroups2) {
+                // Lanes c of a quad hold x rows 0, 1 over group slot c: add the
+                // slots (fixed butterfly order); lane c = 0 then holds columns 0, 1.
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
+                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
+                    if (c != 0) acc[i] = 0.f;
+                }
+            }
+            // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
+            // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
+            if (kh == 1) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+            }
+            named_sync(1, kConsumers * 32);
+            if (kh == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
+            }
+            constexpr bool to_smem = EPI != kEpiPlain;
+            if (complete && to_smem) {
+                // Each kh = 0 thread rewrites the s_red entries it just read.
+                if (kh == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+                }
+                named_sync(1, kConsumers * 32);
+                if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
+                if constexpr (EPI == kEpiArgmax) argmax_out(rb);
+                if constexpr (EPI == kEpiTp) {
+                    tp_finish(rb);
+                } else {
+                    named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
+                }
+                return;
+            }
+            if (complete) {
+                if (kh == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
+                        if (row < p.n && col < p.m) {
+                            if (p.yf) p.yf[(int64_t)col * p.ldy + row] = acc[i];
+                            else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                        }
+                    }
+                }
+                named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
+                return;
+            }
+            const int slot = (rb == first_rb) ? 0 : 1;
+            float* part = p.partial + ((int64_t)blockIdx.x * 2 + slot) * kRows * 8;
+            if (kh == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+            }
+            arrive_partial(rb);
         };
         // nvfp4 unit with group-slot x columns (kXlGroups2): the codes enter
         // the mma unscaled (E2M1 -> f16 is exact); each half super-step (jp
@@ -885,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 flush(rb, complete);
             }
         }
-        if (p.tp_n > 1) tp_complete();
+        if constexpr (EPI == kEpiTp) tp_complete();
         if constexpr (EPI == kEpiArgmax) argmax_finish();
     }
     __syncthreads();
@@ -938,21 +945,21 @@ int pick_kernel(int fmt, int64_t m, int epi, int dev, GemvTcKernel* fn, int* sme
         const char* e = getenv("QMM_XL");
         return e && e[0] == '0';
     }();
-    // One table row per (format / layout) and epilogue.
-    static const GemvTcKernel table[3][3] = {
+    // One table row per (format / layout), one column per epilogue.
+    static const GemvTcKernel table[3][4] = {
         {qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiArgmax>},
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiArgmax>, qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiTp>},
         {qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiArgmax>},
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiArgmax>, qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiTp>},
         {qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiArgmax>},
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiArgmax>, qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiTp>},
     };
     const int row = fmt == kMXFP8 ? 0 : (!tokens_only && m <= 2) ? 1 : 2;
     *smem = fmt == kMXFP8 ? smem_bytes<kMXFP8>() : smem_bytes<kNVFP4>();
     *fn = table[row][epi];
-    const int slot = row * 3 + epi;
+    const int slot = row * 4 + epi;
     static std::mutex mu;
-    static bool configured[9][64] = {};
+    static bool configured[12][64] = {};
     if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!configured[slot][dev]) {
@@ -1129,7 +1136,7 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     cfg.numAttrs = pdl ? 1 : 0;
     GemvTcKernel fn = nullptr;
     int smem = 0;
-    const int epi = a.argmax_ids ? kEpiArgmax : a.swiglu_n > 0 ? kEpiSwiglu : kEpiPlain;
+    const int epi = a.argmax_ids ? kEpiArgmax : a.swiglu_n > 0 ? kEpiSwiglu : p.tp_n > 1 ? kEpiTp : kEpiPlain;
     if (int rc = pick_kernel(fmt, a.m, epi, w->device, &fn, &smem)) return rc;
     cfg.dynamicSmemBytes = smem;
     QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, st->cmap, xmap, p));
