@@ -822,27 +822,24 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                     const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)sb0), s1 = e4m3x2_to_f16x2((uint16_t)sb1);
                     const uint32_t s0lo = __byte_perm(s0, 0, 0x1010), s0hi = __byte_perm(s0, 0, 0x3232);
                     const uint32_t s1lo = __byte_perm(s1, 0, 0x1010), s1hi = __byte_perm(s1, 0, 0x3232);
-                    // Widen whole words: h[b] = f16x2 of byte b (codes 2b, 2b + 1), scaled.
-                    uint32_t h0[16], h1[16];
-                    e2m1x8_to_f16x2(w0.x, *reinterpret_cast<uint32_t(*)[4]>(&h0[0]));
-                    e2m1x8_to_f16x2(w0.y, *reinterpret_cast<uint32_t(*)[4]>(&h0[4]));
-                    e2m1x8_to_f16x2(w0.z, *reinterpret_cast<uint32_t(*)[4]>(&h0[8]));
-                    e2m1x8_to_f16x2(w0.w, *reinterpret_cast<uint32_t(*)[4]>(&h0[12]));
-                    e2m1x8_to_f16x2(w1.x, *reinterpret_cast<uint32_t(*)[4]>(&h1[0]));
-                    e2m1x8_to_f16x2(w1.y, *reinterpret_cast<uint32_t(*)[4]>(&h1[4]));
-                    e2m1x8_to_f16x2(w1.z, *reinterpret_cast<uint32_t(*)[4]>(&h1[8]));
-                    e2m1x8_to_f16x2(w1.w, *reinterpret_cast<uint32_t(*)[4]>(&h1[12]));
-#pragma unroll
-                    for (int b = 0; b < 16; ++b) {
-                        h0[b] = hmul2u(h0[b], b < 8 ? s0lo : s0hi);
-                        h1[b] = hmul2u(h1[b], b < 8 ? s1lo : s1hi);
-                    }
+                    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                     for (int jp = 0; jp < 4; ++jp) {
+                        // Word jp of rows r0 / r1 widened and scaled just before
+                        // its mmas: ha[b] = f16x2 of byte 4 jp + b (codes 2b, 2b + 1).
+                        uint32_t ha[4], hb[4];
+                        e2m1x8_to_f16x2(wa[jp], ha);
+                        e2m1x8_to_f16x2(wb[jp], hb);
+                        const uint32_t sa = jp < 2 ? s0lo : s0hi, sbv = jp < 2 ? s1lo : s1hi;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            ha[b] = hmul2u(ha[b], sa);
+                            hb[b] = hmul2u(hb[b], sbv);
+                        }
                         const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
-                        const uint32_t a0[4] = {h0[4 * jp], h1[4 * jp], h0[4 * jp + 1], h1[4 * jp + 1]};
-                        const uint32_t a1[4] = {h0[4 * jp + 2], h1[4 * jp + 2], h0[4 * jp + 3], h1[4 * jp + 3]};
+                        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
+                        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
                         mma16816(d0, a0, bx.x, bx.y);
                         mma16816(d1, a1, bx.z, bx.w);
                     }
