@@ -14,8 +14,9 @@ its weights from HBM (no L2 flush needed).
   value  whole-job algorithmic GB/s (codes + scales + x + y of the full
          problem, every GEMM) / device time of the K timed steps, max over
          ranks, inputs resident in HBM;
-  e2e    the same metric through the C-ABI call with host buffers: each GEMM
-         copies its x from pinned host memory, runs, and copies y back;
+  e2e    the same metric through the C-ABI call with host buffers: per step
+         each M's x rows come from pinned host memory, every weight copy runs
+         on them (eager C-ABI calls), and each M's y is read back;
   roofline  the GEMV kernel alone: per-launch algorithmic bytes / per-launch
          CUDA-event time against the measured HBM copy bandwidth;
   cpu_baseline  the CPU restatement (oracle, fp32 accumulate, OpenMP) on the
@@ -47,8 +48,8 @@ L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 # Per-launch DRAM traffic of the decode kernel (dram__bytes_read.sum +
 # dram__bytes_write.sum) from an ncu --set full capture of two launches of
-# this bench's decode run (50.22 MB read + 0.06 MB written per launch).
-GEMV_TRAFFIC_BYTES = 50.28e6
+# this bench's decode run (50.26 MB read + 0.05 MB written per launch).
+GEMV_TRAFFIC_BYTES = 50.31e6
 
 
 def _load(name, path):
@@ -604,11 +605,15 @@ def main() -> None:
     y_host = {m: torch.empty((m, N_OUT), dtype=torch.bfloat16).pin_memory() for m in M_SET}
 
     def e2e_step():
-        for wt in weights:
-            for m in M_SET:
-                x_dev[m].copy_(x_host[m], non_blocking=True)
+        # One step's inputs (the x rows of each M) come from pinned host memory
+        # once, every weight copy - a different layer of the stack - runs on
+        # them through the C ABI (eager launches), and each M's result is read
+        # back once: what a decode step exchanges with the host.
+        for m in M_SET:
+            x_dev[m].copy_(x_host[m], non_blocking=True)
+            for wt in weights:
                 gemm(wt, m)
-                y_host[m].copy_(y_dev[m], non_blocking=True)
+            y_host[m].copy_(y_dev[m], non_blocking=True)
 
     e_steps, e_ms = 0, float("nan")
     if not args.no_e2e:
@@ -627,8 +632,8 @@ def main() -> None:
     total_bytes = step_bytes(copies) * args.steps
     value = total_bytes / (ms * 1e-3) / 1e9
     e2e_value = step_bytes(copies) * e_steps / (e_ms * 1e-3) / 1e9 if e_steps else None
-    h2d = copies * sum(m * k_shard * 2 for m in M_SET)
-    d2h = copies * sum(m * N_OUT * 2 for m in M_SET)
+    h2d = sum(m * k_shard * 2 for m in M_SET)
+    d2h = sum(m * N_OUT * 2 for m in M_SET)
 
     # Roofline of the GEMV: per-launch algorithmic bytes of this rank's shard.
     per_launch_bytes = sum(algo_bytes(m, N_OUT, k_shard) for m, _ in k_ms)
