@@ -620,6 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 // keeps 8 contributor loads in flight per batch.
                 const int ifirst = owner(rb * p.kchunks), ilast = owner(rb * p.kchunks + p.kchunks - 1);
                 const int t = threadIdx.x - kFirstConsumer * 32;
+                // Contributor j wrote rb into its slot 0 when rb is its first row
+                // block.  Every contributor after ifirst begins inside rb; ifirst
+                // used slot 1 if its range began in an earlier row block.
+                const int slot_first = first_unit(ifirst) < rb * p.kchunks ? 1 : 0;
                 float v[2] = {0.f, 0.f};
                 for (int j0 = ifirst; j0 <= ilast; j0 += 8) {
                     float ld[8][2];
@@ -628,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const int j = j0 + q;
                         ld[q][0] = ld[q][1] = 0.f;
                         if (j <= ilast) {
-                            const int jslot = (first_unit(j) / p.kchunks == rb) ? 0 : 1;
+                            const int jslot = j == ifirst ? slot_first : 0;
                             const float* src = p.partial + ((int64_t)j * 2 + jslot) * kRows * 8;
                             ld[q][0] = __ldcg(src + t);
                             ld[q][1] = __ldcg(src + t + 512);
