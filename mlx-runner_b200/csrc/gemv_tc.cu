@@ -14,20 +14,25 @@
 //     per-unit scale tiles made at weight creation) and the x chunk with
 //     256-element 2D TMAs, into a 4-stage ring: 128 KB of codes in flight per
 //     SM without spending registers;
-//   - a converter warp turns the x chunk into f16 B fragments after an exact
-//     power-of-two scaling into f16 range (per x row and chunk), so every x
-//     value within 2^29 of the chunk's largest is represented exactly;
+//   - three converter warps turn the x chunk (on a barrier of its own, an L2
+//     hit) into f16 B fragments after an exact power-of-two scaling into f16
+//     range (per x row and chunk), so every x value within 2^29 of the
+//     chunk's largest is represented exactly;
 //   - 16 consumer warps (8 groups of 16 rows x 2 halves of the unit's k
-//     range) run mma.sync.m16n8k16 (f16 in,
-//     fp32 accumulate) with the weight codes widened by cvt.f16x2.e2m1x2 /
-//     .e4m3x2 (exact).  nvfp4 scales multiply the f16 codes (E2M1 x UE4M3 is
-//     exact in f16); mxfp8 scales (any power of two) are applied in fp32 to
-//     per-group partial sums;
+//     range) run mma.sync.m16n8k16 (f16 in, fp32 accumulate) with the weight
+//     codes widened by cvt.f16x2.e2m1x2 / .e4m3x2 (exact), one 32-bit word at
+//     a time.  nvfp4 for M <= 2: the x operand is block-diagonal, each MMA
+//     column holds one group, and the group scale multiplies the fp32 sums;
+//     nvfp4 for M > 2: scales multiply the f16 codes (E2M1 x UE4M3 is exact in
+//     f16); mxfp8 scales (any power of two) are applied in fp32 to per-group
+//     partial sums;
+//   - one kernel instantiation per epilogue: y (bf16, or fp32 partials), the
+//     SwiGLU pair, greedy sampling, or the row-parallel exchange;
 //   - rows of a block split between CTAs are summed by the last CTA to
 //     finish them, in CTA order (deterministic), through a small fp32
 //     scratch owned by the weight; the counters are reset by that CTA.  One
 //     thread per CTA fences (per-thread fences stall under HBM load) and the
-//     final sum keeps 8 loads in flight per thread.
+//     final sum issues every contributor's loads at once.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -809,7 +814,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if constexpr (FMT == kNVFP4 && XL != kXlTokens) {
                 consume_groups(cs, ss, xf, xs0, xs1);
             } else if constexpr (FMT == kNVFP4) {
-                // Two accumulators (even / odd steps) keep two mma chains in flight.
+                // Two accumulators (first / second mma of each word) keep two
+                // mma chains in flight.
                 float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int si = 0; si < 2; ++si) {

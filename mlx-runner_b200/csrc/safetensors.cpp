@@ -271,8 +271,9 @@ bool read_at(int fd, void* dst, uint64_t n, uint64_t off) {
     return true;
 }
 
+// model_dir / file, as weights.zig joins them: shard names from the index
+// are taken relative to the model directory.
 std::string join(const std::string& dir, const std::string& f) {
-    if (!f.empty() && f[0] == '/') return f;
     if (dir.empty()) return f;
     return dir.back() == '/' ? dir + f : dir + "/" + f;
 }
