@@ -121,3 +121,25 @@ def test_no_device_is_an_error_not_a_fallback():
     rc = _mm()
     assert qmm.STATUS_NAMES[rc] in ("CudaError", "NoDevice")
     qmm.take_error()
+
+
+def test_next_row_entry_points_validate_on_host():
+    """SwiGLU, greedy sampling and checkpoint entry points reject bad arguments
+    before any device work."""
+    L = qmm.lib()
+    h = ctypes.c_void_p()
+    spec = qmm.make_spec("nvfp4")
+    qmm.take_error()
+    rc = L.qmm_swiglu_weight_create(None, None, None, None, 0, 32, 0, 0, spec, 0, None, ctypes.byref(h))
+    assert _status(rc) == "BadShape" and not h.value                # n must be > 0
+    rc = L.qmm_swiglu_weight_create(None, None, None, None, 8, 24, 0, 0, spec, 0, None, ctypes.byref(h))
+    assert _status(rc) == "BadShape"                                # k % 16 != 0
+    rc = L.qmm_swiglu_weight_create(None, None, None, None, 8, 32, 0, 0, spec, 0, None, None)
+    assert _status(rc) == "BadArgument"                             # no out pointer
+    assert _status(L.qmm_swiglu_run(None, None, 1, 32, None, 8, None)) == "BadArgument"
+    assert _status(L.qmm_lm_head_argmax(None, None, 1, 32, None, None, None, 0, None)) == "BadArgument"
+    assert _status(L.qmm_checkpoint_open(None, ctypes.byref(h))) == "BadArgument"
+    assert _status(L.qmm_checkpoint_open(b"/nonexistent-model-dir", ctypes.byref(h))) == "IoError"
+    assert not h.value
+    assert L.qmm_checkpoint_close(None) == 0
+    assert _status(L.qmm_checkpoint_load_linear(None, b"x", None, ctypes.byref(h))) == "BadArgument"
