@@ -16,7 +16,8 @@ its weights from HBM (no L2 flush needed).
          ranks, inputs resident in HBM;
   e2e    the same metric through the C-ABI call with host buffers: per step
          each M's x rows come from pinned host memory, every weight copy runs
-         on them (eager C-ABI calls), and each M's y is read back;
+         on them, and each M's y is read back; the step replays as one CUDA
+         graph (copies included), and `eager_value` times eager C-ABI calls;
   roofline  the GEMV kernel alone: per-launch algorithmic bytes / per-launch
          CUDA-event time against the measured HBM copy bandwidth;
   cpu_baseline  the CPU restatement (oracle, fp32 accumulate, OpenMP) on the
@@ -604,34 +605,81 @@ def main() -> None:
     x_host = {m: x_full[m][:, rank * k_shard:(rank + 1) * k_shard].contiguous().pin_memory() for m in M_SET}
     y_host = {m: torch.empty((m, N_OUT), dtype=torch.bfloat16).pin_memory() for m in M_SET}
 
+    copy_stream = torch.cuda.Stream()
+    ev_in = {m: torch.cuda.Event() for m in M_SET}
+    ev_out = {m: torch.cuda.Event() for m in M_SET}
+
     def e2e_step():
         # One step's inputs (the x rows of each M) come from pinned host memory
         # once, every weight copy - a different layer of the stack - runs on
-        # them through the C ABI (eager launches), and each M's result is read
-        # back once: what a decode step exchanges with the host.
+        # them through the C ABI, and each M's result is read back once: what
+        # a decode step exchanges with the host.  The copies run on their own
+        # stream: the uploads go ahead of the compute, and each M's read-back
+        # overlaps the next M's GEMMs; the step ends when the last read-back has.
+        cur = torch.cuda.current_stream()
+        copy_stream.wait_stream(cur)          # the previous step is done with x_dev / y_dev
+        with torch.cuda.stream(copy_stream):
+            for m in M_SET:
+                x_dev[m].copy_(x_host[m], non_blocking=True)
+                ev_in[m].record(copy_stream)
         for m in M_SET:
-            x_dev[m].copy_(x_host[m], non_blocking=True)
+            cur.wait_event(ev_in[m])
             for wt in weights:
                 gemm(wt, m)
-            y_host[m].copy_(y_dev[m], non_blocking=True)
+            ev_out[m].record(cur)
+            copy_stream.wait_event(ev_out[m])
+            with torch.cuda.stream(copy_stream):
+                y_host[m].copy_(y_dev[m], non_blocking=True)
+        cur.wait_stream(copy_stream)
 
-    e_steps, e_ms = 0, float("nan")
+    e_steps, e_ms, e_ms_eager, e2e_mode = 0, float("nan"), float("nan"), "eager"
     if not args.no_e2e:
         for _ in range(max(1, args.warmup)):
             e2e_step()
         barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_steps = max(1, min(args.steps, 50))
-        e0.record(stream)
-        for _ in range(e_steps):
-            e2e_step()
-        e1.record(stream)
-        barrier()
-        e_ms = max_over_ranks(e0.elapsed_time(e1))
+
+        def time_e2e(run) -> float:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(e_steps):
+                run()
+            e1.record(stream)
+            barrier()
+            return max_over_ranks(e0.elapsed_time(e1))
+        e_ms_eager = time_e2e(e2e_step)
+        e_ms = e_ms_eager
+        if graphs:
+            # The same step - host copies, every C-ABI call, the read-back - as
+            # one CUDA graph, the way a serving loop replays a decode step.
+            ok = True
+            try:
+                cap = torch.cuda.Stream()
+                cap.wait_stream(stream)
+                graphs["e2e"] = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graphs["e2e"], stream=cap):
+                    e2e_step()
+                torch.cuda.synchronize()
+            except Exception as exc:
+                ok = False
+                graphs.pop("e2e", None)
+                print(f"bench: e2e graph capture failed ({exc}); e2e stays eager", file=sys.stderr)
+            if world > 1:                     # every rank takes the same path
+                t = torch.tensor([1.0 if ok else 0.0], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MIN)
+                ok = t.item() >= 1.0
+            if ok:
+                graphs["e2e"].replay()
+                barrier()
+                e_ms = time_e2e(graphs["e2e"].replay)
+                e2e_mode = "cuda_graph"
+            else:
+                graphs.pop("e2e", None)
 
     total_bytes = step_bytes(copies) * args.steps
     value = total_bytes / (ms * 1e-3) / 1e9
     e2e_value = step_bytes(copies) * e_steps / (e_ms * 1e-3) / 1e9 if e_steps else None
+    e2e_eager = step_bytes(copies) * e_steps / (e_ms_eager * 1e-3) / 1e9 if e_steps else None
     h2d = sum(m * k_shard * 2 for m in M_SET)
     d2h = sum(m * N_OUT * 2 for m in M_SET)
 
@@ -670,7 +718,7 @@ def main() -> None:
                          "kernel": "qmm_gemv_tc_kernel<nvfp4>", "per_m_us": {
                              str(m): 1e3 * statistics.mean(t for mm, t in k_ms if mm == m) for m in M_SET}},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e_steps},
+                    "steps": e_steps, "launch": e2e_mode, "eager_value": e2e_eager},
             "gpu_launches": args.steps * copies * len(M_SET) * launches_per_gemm,
             "clocks": clocks,
             "prefill": prefill,
