@@ -182,16 +182,25 @@ CONFIG = {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], 
 PREFILL = {"m": 32768, "n": 34816, "k": 5120, "mode": "nvfp4"}
 
 
-def prefill_measure(args, qmm, oracle, dev, world: int, rank: int, barrier, max_over_ranks) -> dict:
+def _quantized_normal(qmm, n: int, k: int, mode: str, dev, seed: int):
+    """W ~ N(0, 0.02^2) fp32 [n, k] drawn on the GPU (seeded) and quantized
+    there by qmm_quantize: the packed codes and scales of a synthetic weight."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.randn((n, k), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+    codes, scales = qmm.quantize(w, mode)
+    del w
+    return codes, scales
+
+
+def prefill_measure(args, qmm, dev, world: int, rank: int, barrier, max_over_ranks) -> dict:
     """BASELINE config 3 (32k-token nvfp4 gate/up GEMM) on the tcgen05 kernel;
     N-sharded (column-parallel, no collective) over the GPUs."""
     import torch
     m, n, k, mode = args.prefill_m, PREFILL["n"], PREFILL["k"], PREFILL["mode"]
-    rng = np.random.default_rng(2)
-    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
-    codes, scales = oracle.quantize(w, mode)
-    del w
+    codes, scales = _quantized_normal(qmm, n, k, mode, dev, seed=2)
     wt = qmm.QuantizedWeight(codes, scales, mode, shard=(0, rank, world))
+    del codes, scales
     g = torch.Generator(device=dev).manual_seed(3)
     x = torch.randn((m, k), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     y = torch.empty((m, wt.n), dtype=torch.bfloat16, device=dev)
@@ -394,6 +403,131 @@ def next_rows_measure(args, qmm, dev) -> dict:
     return out
 
 
+# the linear stack of one decode step of a 64-layer
+# hybrid (hidden 5120, FFN 17408, vocab 248320), nvfp4, M = 3 (MTP verify).
+GDN_LINEARS = (("in_proj_qkv", 10240, 5120), ("in_proj_z", 6144, 5120), ("in_proj_b", 48, 5120),
+               ("in_proj_a", 48, 5120), ("out_proj", 5120, 6144))
+ATTN_LINEARS = (("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120), ("o_proj", 5120, 6144))
+MLP_FFN, HIDDEN, VOCAB = 17408, 5120, 248320
+# the prefill GEMMs of one GDN layer, mxfp8, T = 32768.
+GDN_PREFILL = (("in_proj_qkvz", 16384, 5120), ("in_proj_ba", 96, 5120), ("out_proj", 5120, 6144),
+               ("gate_up", 34816, 5120), ("down", 5120, 17408))
+
+
+def configs_measure(args, qmm, dev) -> dict:
+    """BASELINE configs 1, 4 and 5 on one GPU, each through the C-ABI calls,
+    with weights ~N(0, 0.02^2) quantized on the GPU by qmm_quantize:
+      cfg1  mxfp8 GEMV x [1, 5120] . W[17408, 5120]^T; weight copies rotate
+            (inputs larger than L2), CUDA-graph replays;
+      cfg4  the five mxfp8 prefill GEMMs of a GDN layer at T = 32768, each
+            timed alone (x and y far larger than L2);
+      cfg5  one decode step's linear stack, nvfp4, M = 3: 48 GDN layers
+            (qkv, z, b, a, out_proj, gate/up with the SwiGLU epilogue, down),
+            16 attention layers (q, k, v, o, the same MLP) and lm_head -
+            433 launches as one CUDA graph over 14.4 GB of distinct weight
+            buffers (each layer's buffers hold a copy of one quantized draw
+            per shape)."""
+    import torch
+    out = {}
+    peak, peak_kind = peaks()
+    tpeak, tpeak_kind = bf16_peak()
+    bf = torch.bfloat16
+
+    # Config 1.
+    n, k = 17408, 5120
+    codes, scales = _quantized_normal(qmm, n, k, "mxfp8", dev, seed=10)
+    wbytes = n * k + n * k // 32
+    copies = max(4, -(-4 * L2_BYTES // wbytes))
+    ws = [qmm.QuantizedWeight(codes, scales, "mxfp8") for _ in range(copies)]
+    del codes, scales
+    x = torch.randn((1, k), device=dev).to(bf)
+    y = torch.empty((1, n), device=dev, dtype=bf)
+
+    def c1(st):
+        for w in ws:
+            w.run(x, out=y, stream=st)
+    us = 1e3 * _graph_ms(c1, 20) / copies
+    b1 = wbytes + 2 * k + 2 * n
+    out["cfg1"] = {"workload": "cfg1: mxfp8 GEMV x [1, 5120] . W[17408, 5120]^T", "us": us,
+                   "GBs": b1 / (us * 1e-6) / 1e9, "frac": b1 / (us * 1e-6) / 1e9 / peak, "peak": peak,
+                   "peak_kind": peak_kind, "algo_bytes": b1,
+                   "l2": f"{copies} weight copies x {wbytes / 1e6:.1f} MB rotate (larger than L2)"}
+    for w in ws:
+        w.close()
+    del ws
+
+    # Config 4.
+    t = args.prefill_m
+    gemms, tot_flops, tot_ms = {}, 0.0, 0.0
+    for i, (name, n, k) in enumerate(GDN_PREFILL):
+        codes, scales = _quantized_normal(qmm, n, k, "mxfp8", dev, seed=20 + i)
+        w = qmm.QuantizedWeight(codes, scales, "mxfp8")
+        del codes, scales
+        x = torch.randn((t, k), device=dev).to(bf)
+        y = torch.empty((t, n), device=dev, dtype=bf)
+        ms = _graph_ms(lambda st: w.run(x, out=y, stream=st), 3)
+        flops = 2.0 * t * n * k
+        nbytes = t * k * 2 + t * n * 2 + n * k + n * k // 32
+        gemms[name] = {"n": n, "k": k, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                       "GBs": nbytes / (ms * 1e-3) / 1e9}
+        tot_flops += flops
+        tot_ms += ms
+        w.close()
+        del w, x, y
+    out["cfg4"] = {"workload": f"cfg4: mxfp8 GDN-layer prefill GEMMs, T = {t}", "gemms": gemms,
+                   "total_ms": tot_ms, "tflops": tot_flops / (tot_ms * 1e-3) / 1e12,
+                   "frac": tot_flops / (tot_ms * 1e-3) / 1e12 / tpeak, "peak": tpeak, "peak_kind": tpeak_kind,
+                   "note": "in_proj_ba (N = 96) is bound by reading x: see its GBs"}
+
+    # Config 5.
+    m = 3
+    shapes = {name: (n, k) for name, n, k in GDN_LINEARS + ATTN_LINEARS}
+    shapes.update({"down": (HIDDEN, MLP_FFN), "lm_head": (VOCAB, HIDDEN)})
+    draws = {name: _quantized_normal(qmm, n, k, "nvfp4", dev, seed=40 + i) for i, (name, (n, k)) in enumerate(shapes.items())}
+    gate = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=60)
+    up = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=61)
+    layers = []
+    for li in range(64):
+        names = [nm for nm, _, _ in (ATTN_LINEARS if li % 4 == 3 else GDN_LINEARS)] + ["down"]
+        lay = {nm: qmm.QuantizedWeight(*draws[nm], "nvfp4") for nm in names}
+        lay["mlp"] = qmm.SwiGLUWeight(*gate, *up, "nvfp4")
+        layers.append(lay)
+    lm = qmm.QuantizedWeight(*draws["lm_head"], "nvfp4")
+    del draws, gate, up
+    xh = torch.randn((m, HIDDEN), device=dev).to(bf)
+    x6 = torch.randn((m, 6144), device=dev).to(bf)
+    outs = {nm: torch.empty((m, n), device=dev, dtype=bf) for nm, (n, _) in shapes.items()}
+    hbuf = torch.empty((m, MLP_FFN), device=dev, dtype=bf)
+    launches = sum(len(lay) for lay in layers) + 1
+
+    def c5(st):
+        # Every projection of the step; the non-linear ops between them (norms,
+        # the GDN recurrence, attention) are not this path: each projection
+        # reads a fixed input of its shape, down reads the SwiGLU output.
+        for lay in layers:
+            for nm, w in lay.items():
+                if nm == "mlp":
+                    w.run(xh, out=hbuf, stream=st)
+                elif nm == "down":
+                    w.run(hbuf, out=outs["down"], stream=st)
+                else:
+                    w.run(x6 if w.k == 6144 else xh, out=outs[nm], stream=st)
+        lm.run(xh, out=outs["lm_head"], stream=st)
+    ms = _graph_ms(c5, 5)
+    elems = sum(lay_w.n * lay_w.k * (2 if nm == "mlp" else 1) for lay in layers for nm, lay_w in lay.items())
+    elems += VOCAB * HIDDEN
+    wb = elems * 9 // 16
+    out["cfg5"] = {"workload": "cfg5: decode-step linear stack, 64-layer hybrid, nvfp4, M = 3, 1 GPU",
+                   "weight_elements": elems, "weight_bytes": wb, "launches": launches, "step_ms": ms,
+                   "GBs": wb / (ms * 1e-3) / 1e9, "frac": wb / (ms * 1e-3) / 1e9 / peak, "peak": peak,
+                   "peak_kind": peak_kind, "tflops": 2.0 * m * elems / (ms * 1e-3) / 1e12}
+    for lay in layers:
+        for w in lay.values():
+            w.close()
+    lm.close()
+    return out
+
+
 def bf16_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -441,6 +575,7 @@ def main() -> None:
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-warmup", type=int, default=2)
     ap.add_argument("--no-next", action="store_true", help="skip the SwiGLU / lm_head / MTP-graph measurements")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 4 / 5 measurements")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -458,7 +593,6 @@ def main() -> None:
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     qmm = _load("qmm", os.path.join(PKG, "qmm.py"))
-    oracle = _load("oracle", os.path.join(ROOT, "oracle", "oracle.py"))
 
     def barrier():
         if world > 1:
@@ -473,7 +607,7 @@ def main() -> None:
         return float(t.item())
 
     if args.prefill_only:
-        pf = prefill_measure(args, qmm, oracle, dev, world, rank, barrier, max_over_ranks)
+        pf = prefill_measure(args, qmm, dev, world, rank, barrier, max_over_ranks)
         if rank == 0:
             print(json.dumps({"prefill": pf}), flush=True)
         if world > 1:
@@ -481,15 +615,14 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
-    # Weights: identical on every rank (seed 0), K-sharded by rank.
-    rng = np.random.default_rng(0)
-    w_full = (rng.standard_normal((N_OUT, K_IN), dtype=np.float32) * 0.02).astype(np.float32)
-    codes, scales = oracle.quantize(w_full, MODE)
-    del w_full
+    # Weights: identical on every rank (seed 0, drawn and quantized on the
+    # GPU by qmm_quantize), K-sharded by rank.
+    codes, scales = _quantized_normal(qmm, N_OUT, K_IN, MODE, dev, seed=0)
     k_shard = K_IN // world
     shard_bytes = algo_bytes(0, N_OUT, k_shard)
     copies = max(4, -(-4 * L2_BYTES // shard_bytes))
     weights = [qmm.QuantizedWeight(codes, scales, MODE, shard=(1, rank, world)) for _ in range(copies)]
+    del codes, scales
     comm = None
     if world > 1:
         uid = [qmm.TPComm.unique_id() if rank == 0 else None]
@@ -697,17 +830,20 @@ def main() -> None:
     weights = []
     prefill = None
     if not args.no_prefill:
-        prefill = prefill_measure(args, qmm, oracle, dev, world, rank, barrier, max_over_ranks)
+        prefill = prefill_measure(args, qmm, dev, world, rank, barrier, max_over_ranks)
     next_rows = None
     if not args.no_next and world == 1:
         next_rows = next_rows_measure(args, qmm, dev)
+    configs = None
+    if not args.no_configs and world == 1:
+        configs = configs_measure(args, qmm, dev)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4xbf16->f32acc",
-            "data": "synthetic (seeded N(0,1) x, N(0,0.02^2) W quantized by the oracle's NVFP4 rule)",
+            "data": "synthetic (seeded N(0,1) x; N(0,0.02^2) W drawn and quantized on the GPU by qmm_quantize)",
             "config": dict(CONFIG, copies=copies, parallelism=f"tp{world} (K-shard)" if world > 1 else "none",
                            launch=launch_mode,
                            l2=f"inputs larger than L2: {copies} weight copies x {shard_bytes / 1e6:.1f} MB rotate"),
@@ -723,6 +859,7 @@ def main() -> None:
             "clocks": clocks,
             "prefill": prefill,
             "next_rows": next_rows,
+            "configs": configs,
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()

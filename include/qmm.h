@@ -21,6 +21,7 @@
  * Reference interfaces replaced (paths relative to the mlx-runner tree):
  *   src/mlx.zig:265      mlx_quantized_matmul    -> qmm_quantized_matmul, qmm_run
  *   src/mlx.zig:274      mlx_dequantize          -> qmm_dequantize
+ *   src/mlx.zig:278      mlx_quantize            -> qmm_quantize
  *   src/mlx.zig:41-51    mlx_optional_int        -> qmm_optional_int
  *   src/mlx.zig:589-595  check (int status)      -> qmm_status return codes
  *   src/mlx.zig:719-805  error latch             -> qmm_last_error, qmm_error_pending
@@ -286,6 +287,24 @@ int qmm_lm_head_argmax(const qmm_weight* w, const void* x_dev, int64_t m, int64_
  * (F32).  Every mxfp8/nvfp4 value is exact in fp32; bf16 is exact unless a
  * value leaves bf16's range. */
 int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dtype, void* stream);
+
+/* src/mlx.zig:278 mlx_quantize, as the reference's qmm test calls it
+ * (src/model.zig:1577: mode "mxfp8" / "nvfp4", global_scale NULL): w [N, K]
+ * (w_dtype F32 or BF16, row stride ldw elements, 0 = K) on the device ->
+ * codes U32 [N, K*bits/32] (LSB-first) and scales U8 [N, K/group], dense,
+ * on `stream`; (group_size, bits, mode) resolve as in qmm_spec_from_args and
+ * global_scale must be NULL.  Per group, amax = the largest magnitude (NaN
+ * skipped):
+ *   mxfp8 (OCP MX v1.0): X = floor(log2 amax) - 8 clamped to [-127, 127]
+ *     (-127 for amax 0, -9 for an infinite amax), scale byte X + 127,
+ *     code = E4M3(w * 2^-X);
+ *   nvfp4: scale = E4M3(amax / 6), code = E2M1(w / scale) (0 if scale is 0).
+ * E4M3 / E2M1 round to nearest even and saturate (448, 6); NaN is 0x7F
+ * (E4M3) or sign|7 (E2M1).  Deterministic and bit-identical to the CPU
+ * restatement of these rules. */
+int qmm_quantize(const void* w_dev, int32_t w_dtype, int64_t n, int64_t k, int64_t ldw,
+                 qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
+                 const void* global_scale, uint32_t* codes_dev, uint8_t* scales_dev, void* stream);
 
 /* ---- tensor parallel (NCCL over NVLink) ----------------------------------- */
 

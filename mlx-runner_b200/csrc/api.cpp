@@ -598,6 +598,33 @@ extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dt
                           static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int qmm_quantize(const void* w_dev, int32_t w_dtype, int64_t n, int64_t k, int64_t ldw,
+                            qmm_optional_int group_size, qmm_optional_int bits, const char* mode,
+                            const void* global_scale, uint32_t* codes_dev, uint8_t* scales_dev, void* stream) {
+    QMM_FAULT_POINT("qmm_quantize");
+    qmm_quant_spec spec;
+    if (int rc = qmm_spec_from_args(group_size, bits, mode, &spec)) return rc;
+    if (global_scale) return set_error(QMM_ERR_BAD_ARGUMENT, "%s quantize takes no global scale", mode);
+    if (w_dtype != QMM_DTYPE_BF16 && w_dtype != QMM_DTYPE_F32)
+        return set_error(QMM_ERR_UNSUPPORTED_DTYPE, "quantize input dtype %d (BF16 or F32)", w_dtype);
+    if (n < 0) return set_error(QMM_ERR_BAD_SHAPE, "n=%lld < 0", (long long)n);
+    if (k <= 0 || k % spec.group_size)
+        return set_error(QMM_ERR_BAD_SHAPE, "k=%lld is not a positive multiple of group %d", (long long)k,
+                         spec.group_size);
+    if (ldw == 0) ldw = k;
+    if (ldw < k) return set_error(QMM_ERR_BAD_SHAPE, "ldw=%lld < k=%lld", (long long)ldw, (long long)k);
+    if (n == 0) return QMM_OK;
+    if (!w_dev || !codes_dev || !scales_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "w, codes or scales is NULL");
+    const int64_t esize = w_dtype == QMM_DTYPE_BF16 ? 2 : 4;
+    if (reinterpret_cast<uintptr_t>(w_dev) % esize)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "w is not %lld-byte aligned", (long long)esize);
+    if (reinterpret_cast<uintptr_t>(codes_dev) & 3) return set_error(QMM_ERR_BAD_ARGUMENT, "codes are not 4-byte aligned");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    return launch_quantize(format_of(spec), w_dev, w_dtype == QMM_DTYPE_BF16, ldw, n, k,
+                           reinterpret_cast<uint8_t*>(codes_dev), scales_dev, static_cast<cudaStream_t>(stream));
+}
+
 // Used by tp.cpp: the row-parallel partial product in fp32.
 namespace qmm {
 // Row-parallel decode with the cross-rank sum fused into the decode kernel.

@@ -106,6 +106,11 @@ int launch_dequant(int fmt, const uint8_t* codes, int64_t ldc, const uint8_t* sc
                    int64_t lds, int64_t n, int64_t k, void* out, bool out_bf16,
                    cudaStream_t stream);
 
+// Quantize w[n][ldw] (fp32, or bf16 when w_bf16) into MLX's packed codes
+// [n][k*bits/8] bytes and scales [n][k/group] (quantize.cu).
+int launch_quantize(int fmt, const void* w, bool w_bf16, int64_t ldw, int64_t n, int64_t k, uint8_t* codes,
+                    uint8_t* scales, cudaStream_t stream);
+
 // Prefill GEMM (m > 8) on the tcgen05 tensor cores.  Returns QMM_OK or an
 // error; *handled = false when the shape is outside the kernel's envelope
 // (the caller then uses the GEMV path over row blocks).

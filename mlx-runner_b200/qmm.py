@@ -44,7 +44,7 @@ EXPORTS = (
     "qmm_abi_version", "qmm_infer_quant_spec", "qmm_mode_str", "qmm_spec_from_args",
     "qmm_quantized_matmul", "qmm_quantized_matmul_noalloc", "qmm_weight_create", "qmm_weight_create_shard", "qmm_shard_range",
     "qmm_weight_destroy",
-    "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_tp_unique_id",
+    "qmm_weight_info", "qmm_run", "qmm_linear", "qmm_dequantize", "qmm_quantize", "qmm_tp_unique_id",
     "qmm_swiglu_weight_create", "qmm_swiglu_run", "qmm_lm_head_argmax",
     "qmm_checkpoint_open", "qmm_checkpoint_close", "qmm_checkpoint_spec", "qmm_checkpoint_tensors",
     "qmm_checkpoint_read", "qmm_checkpoint_load_linear", "qmm_checkpoint_load_swiglu",
@@ -115,6 +115,8 @@ def lib() -> ctypes.CDLL:
     L.qmm_run.argtypes = [vp, vp, i64, i64, vp, i64, ctypes.c_bool, vp]
     L.qmm_linear.argtypes = [vp, ctypes.c_bool, vp, i64, i64, vp, i64, vp]
     L.qmm_dequantize.argtypes = [vp, vp, ctypes.c_int32, vp]
+    L.qmm_quantize.argtypes = [vp, ctypes.c_int32, i64, i64, i64, OptionalInt, OptionalInt, ctypes.c_char_p, vp,
+                               vp, vp, vp]
     L.qmm_swiglu_weight_create.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, QuantSpec, i32, vp,
                                            ctypes.POINTER(vp)]
     L.qmm_swiglu_run.argtypes = [vp, vp, i64, i64, vp, i64, vp]
@@ -270,6 +272,33 @@ def quantized_matmul_noalloc(x, w, scales, out, biases=None, transpose: bool = T
         None if biases is None else biases.data_ptr(), transpose, OptionalInt.of(group_size),
         OptionalInt.of(bits), mode.encode(), _stream_handle(stream)))
     return out
+
+
+def quantize(w, mode: str = "mxfp8", group_size: Optional[int] = None, bits: Optional[int] = None,
+             global_scale=None, stream=None):
+    """src/mlx.zig:278 mlx_quantize (as src/model.zig:1577 calls it): w fp32 or
+    bf16 [N, K] on the GPU -> (codes, scales) on the same device, codes the
+    U32 [N, K*bits/32] words held in an int32 tensor, scales uint8
+    [N, K/group]; the layout QuantizedWeight and quantized_matmul take."""
+    torch = _torch()
+    if w.dtype == torch.float32:
+        dt = DTYPES["F32"]
+    elif w.dtype == torch.bfloat16:
+        dt = DTYPES["BF16"]
+    else:
+        raise QmmError(5, f"quantize input must be float32 or bfloat16, got {w.dtype}")
+    if w.dim() != 2:
+        raise QmmError(1, f"quantize takes a 2-D weight, got shape {tuple(w.shape)}")
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    spec = spec_from_args(group_size, bits, mode)
+    n, k = w.shape
+    codes = torch.empty((n, k * spec.bits // 32), dtype=torch.int32, device=w.device)
+    scales = torch.empty((n, k // spec.group_size), dtype=torch.uint8, device=w.device)
+    check(lib().qmm_quantize(w.data_ptr(), dt, n, k, w.stride(0), OptionalInt.of(group_size), OptionalInt.of(bits),
+                             mode.encode(), None if global_scale is None else global_scale.data_ptr(),
+                             codes.data_ptr(), scales.data_ptr(), _stream_handle(stream)))
+    return codes, scales
 
 
 @dataclass

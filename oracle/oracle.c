@@ -146,7 +146,12 @@ int orc_quantize(int mode, const float* w, int64_t n, int64_t k,
         for (int64_t g = 0; g < ng; ++g) {
             const float* v = wr + g * group;
             float amax = 0.f;
-            for (int i = 0; i < group; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            /* Every NaN is skipped, signalling ones too (a compare, not
+             * fmaxf, whose C library may propagate a signalling NaN). */
+            for (int i = 0; i < group; ++i) {
+                const float a = fabsf(v[i]);
+                if (a > amax) amax = a;
+            }
             if (mode == ORC_MXFP8) {
                 /* OCP MX v1.0: X = 2^(floor(log2(amax)) - emax_elem), emax(E4M3) = 8 */
                 int se = -127;

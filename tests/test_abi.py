@@ -143,3 +143,30 @@ def test_next_row_entry_points_validate_on_host():
     assert not h.value
     assert L.qmm_checkpoint_close(None) == 0
     assert _status(L.qmm_checkpoint_load_linear(None, b"x", None, ctypes.byref(h))) == "BadArgument"
+
+
+def test_quantize_validates_on_host():
+    """qmm_quantize (src/mlx.zig:278) rejects bad arguments before any device
+    work, with the reference's error classes."""
+    L = qmm.lib()
+    O = qmm.OptionalInt.of
+    qmm.take_error()
+    buf = ctypes.c_void_p(16)   # never dereferenced: every call below fails first
+    args = lambda **kw: dict(dict(w=buf, dt=1, n=8, k=32, ldw=0, g=O(None), b=O(None), mode=b"nvfp4", gs=None,
+                                  c=buf, s=buf), **kw)
+
+    def call(**kw):
+        a = args(**kw)
+        return _status(L.qmm_quantize(a["w"], a["dt"], a["n"], a["k"], a["ldw"], a["g"], a["b"], a["mode"], a["gs"],
+                                      a["c"], a["s"], None))
+    assert call(mode=b"affine") == "BadMode"              # as qmm_spec_from_args for every entry point
+    assert call(mode=b"nvfp4", g=O(32)) == "BadMode"
+    assert call(gs=buf) == "BadArgument"                 # global_scale is not taken
+    assert call(dt=2) == "UnsupportedDtype"              # U32 input
+    assert call(k=24) == "BadShape"                      # k % 16
+    assert call(mode=b"mxfp8", k=48) == "BadShape"       # k % 32
+    assert call(ldw=16) == "BadShape"                    # ldw < k
+    assert call(n=-1) == "BadShape"
+    assert call(w=None) == "BadArgument"
+    assert call(c=ctypes.c_void_p(18)) == "BadArgument"  # codes not 4-byte aligned
+    assert call(n=0) == 0                                # empty: nothing to do
