@@ -4,7 +4,13 @@ Headline workload (the config the metric is quoted on):
 nvfp4 small-batch GEMM for decode + MTP verify, x bf16 [M, 17408] with
 M = 1, 2, 3, 4, W [5120, 17408] nvfp4 (E2M1 codes, group 16, UE4M3 scales).
 On N GPUs the weight is K-sharded (row-parallel): every rank multiplies its
-K/N slice and the fp32 partials are summed with one NCCL all-reduce.
+K/N slice and the fp32 partials are summed across ranks inside the decode
+kernel over NVLink (one NCCL all-reduce where that path does not apply).
+
+Beside the headline (one JSON object each): config 3's prefill GEMM
+(N-sharded over the GPUs), the next rows (SwiGLU, lm_head sampling, the MTP
+graph; 1 GPU), configs 1, 4 and 5 and the quantizer on 1 GPU, and config 5
+tensor-parallel on N > 1 GPUs.
 
 A step is one pass of the hot path over one batch of synthetic input: the
 four GEMMs (M = 1..4) against each of C resident weight copies, where the
@@ -578,6 +584,110 @@ def configs_measure(args, qmm, dev) -> dict:
     return out
 
 
+def cfg5_tp_measure(qmm, dev, world: int, rank: int, comm, barrier, max_over_ranks, sum_over_ranks) -> dict:
+    """BASELINE config 5 tensor-parallel over `world` GPUs, one rank each:
+    column-parallel in_proj (qkv|z|b|a), q|k|v, gate / up (SwiGLU) and
+    lm_head - each rank holds its rows of every tensor, no collective;
+    row-parallel out_proj, o_proj and down - each rank holds a K-slice and
+    the fp32 partial sums are added across ranks inside the decode kernel
+    over NVLink (qmm_tp_run_rowparallel): 128 cross-rank sums per step.
+    k_proj / v_proj are replicated when the ranks outnumber the 4 KV heads.
+    One CUDA graph per rank (257 launches), timed as the max over ranks;
+    `GBs` counts the weight bytes all ranks stream."""
+    import torch
+    m, bf = 3, torch.bfloat16
+    shapes = {name: (n, k) for name, n, k in GDN_LINEARS + ATTN_LINEARS}
+    shapes.update({"down": (HIDDEN, MLP_FFN), "lm_head": (VOCAB, HIDDEN)})
+    # Full draws, identical on every rank (same seeds); each rank keeps its shard.
+    draws = {name: _quantized_normal(qmm, n, k, "nvfp4", dev, seed=40 + i) for i, (name, (n, k)) in enumerate(shapes.items())}
+    gate = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=60)
+    up = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=61)
+
+    def rows_of(pair, replicate=False):
+        codes, scales = pair
+        if replicate:
+            return codes, scales
+        r0, nr, _, _ = qmm.shard_range(codes.shape[0], HIDDEN, "nvfp4", 0, rank, world)
+        return codes[r0:r0 + nr], scales[r0:r0 + nr]
+
+    def cat(pairs):
+        return torch.cat([c for c, _ in pairs]), torch.cat([s for _, s in pairs])
+
+    kv_rep = world > 4
+    gdn_in = cat([rows_of(draws[nm]) for nm, _, _ in GDN_LINEARS[:4]])
+    attn_in = cat([rows_of(draws["q_proj"]), rows_of(draws["k_proj"], kv_rep), rows_of(draws["v_proj"], kv_rep)])
+    g_sh, u_sh = rows_of(gate), rows_of(up)
+    lm = qmm.QuantizedWeight(*rows_of(draws["lm_head"]), "nvfp4")
+    layers = []
+    for li in range(64):
+        attn = li % 4 == 3
+        layers.append((qmm.QuantizedWeight(*(attn_in if attn else gdn_in), "nvfp4"),
+                       qmm.QuantizedWeight(*draws["o_proj" if attn else "out_proj"], "nvfp4", shard=(1, rank, world)),
+                       qmm.SwiGLUWeight(*g_sh, *u_sh, "nvfp4"),
+                       qmm.QuantizedWeight(*draws["down"], "nvfp4", shard=(1, rank, world))))
+    del draws, gate, up, gdn_in, attn_in, g_sh, u_sh
+    xh = torch.randn((m, HIDDEN), device=dev).to(bf)
+    x6 = torch.randn((m, 6144 // world), device=dev).to(bf)       # this rank's K-slice of the o/out input
+    hbuf = torch.empty((m, layers[0][2].n), device=dev, dtype=bf)  # this rank's SwiGLU rows = down's K-slice
+    y_in = {id(w): torch.empty((m, w.n), device=dev, dtype=bf) for w in {lay[0] for lay in layers}}
+    y_o = torch.empty((m, HIDDEN), device=dev, dtype=bf)
+    y_d = torch.empty((m, HIDDEN), device=dev, dtype=bf)
+    ylm = torch.empty((m, lm.n), device=dev, dtype=bf)
+
+    def step(st):
+        for w_in, w_o, w_mlp, w_down in layers:
+            w_in.run(xh, out=y_in[id(w_in)], stream=st)
+            comm.run_rowparallel(w_o, x6, out=y_o, stream=st)
+            w_mlp.run(xh, out=hbuf, stream=st)
+            comm.run_rowparallel(w_down, hbuf, out=y_d, stream=st)
+        lm.run(xh, out=ylm, stream=st)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step(s)
+        step(s)
+    s.synchronize()
+    graph, ok = None, True
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step(s)
+        torch.cuda.synchronize()
+    except Exception as exc:
+        ok = False
+        print(f"bench: cfg5 graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+    t = torch.tensor([1.0 if ok else 0.0], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+    use_graph = t.item() >= 1.0
+    run = graph.replay if use_graph else (lambda: step(torch.cuda.current_stream()))
+    run()
+    barrier()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / reps
+    qmm.device_status()
+    elems = sum(w.n * w.k * (2 if i == 2 else 1) for lay in layers for i, w in enumerate(lay)) + lm.n * lm.k
+    all_elems = sum_over_ranks(float(elems))
+    wb = all_elems * 9 / 16
+    peak, peak_kind = peaks()
+    graph = None
+    for lay in layers:
+        for w in lay:
+            w.close()
+    lm.close()
+    return {"workload": f"cfg5: decode-step linear stack, 64-layer hybrid, nvfp4, M = 3, tp{world}",
+            "launches": 4 * len(layers) + 1, "row_parallel_sums": 2 * len(layers), "step_ms": ms,
+            "launch": "cuda_graph" if use_graph else "eager", "weight_bytes_all_ranks": wb,
+            "GBs": wb / (ms * 1e-3) / 1e9, "frac_per_gpu": wb / world / (ms * 1e-3) / 1e9 / peak,
+            "peak": peak, "peak_kind": peak_kind, "kv_replicated": kv_rep}
+
+
 def bf16_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -887,6 +997,12 @@ def main() -> None:
     configs = None
     if not args.no_configs and world == 1:
         configs = configs_measure(args, qmm, dev)
+    elif not args.no_configs and comm is not None:
+        def sum_over_ranks(v: float) -> float:
+            t = torch.tensor([v], dtype=torch.float64, device=dev)
+            dist.all_reduce(t)
+            return float(t.item())
+        configs = {"cfg5": cfg5_tp_measure(qmm, dev, world, rank, comm, barrier, max_over_ranks, sum_over_ranks)}
 
     if rank == 0:
         line = {
