@@ -181,7 +181,7 @@ def run_reference(args, rank: int) -> None:
 
 METRIC = "qmm HBM GB/s, nvfp4 M=1..4 decode/MTP GEMM (K=17408, N=5120)"
 CONFIG = {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], W [5120, 17408], "
-                      "K-sharded over the GPUs with an fp32 all-reduce",
+                      "K-sharded over the GPUs, fp32 partials summed across ranks",
           "mode": MODE, "m": list(M_SET), "n": N_OUT, "k": K_IN}
 
 
@@ -603,21 +603,22 @@ def cfg5_tp_measure(qmm, dev, world: int, rank: int, comm, barrier, max_over_ran
     gate = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=60)
     up = _quantized_normal(qmm, MLP_FFN, HIDDEN, "nvfp4", dev, seed=61)
 
-    def rows_of(pair, replicate=False):
-        codes, scales = pair
-        if replicate:
-            return codes, scales
-        r0, nr, _, _ = qmm.shard_range(codes.shape[0], HIDDEN, "nvfp4", 0, rank, world)
-        return codes[r0:r0 + nr], scales[r0:r0 + nr]
+    tp_plan = _load("tp_plan", os.path.join(PKG, "tp_plan.py"))
+
+    def col(name, pair):
+        # This rank's rows of a column-parallel tensor (all of a replicated one).
+        assert tp_plan.placement(name, world) in ("column", "replicated")
+        return tp_plan.take(*pair, "nvfp4", name, rank, world)
 
     def cat(pairs):
         return torch.cat([c for c, _ in pairs]), torch.cat([s for _, s in pairs])
 
-    kv_rep = world > 4
-    gdn_in = cat([rows_of(draws[nm]) for nm, _, _ in GDN_LINEARS[:4]])
-    attn_in = cat([rows_of(draws["q_proj"]), rows_of(draws["k_proj"], kv_rep), rows_of(draws["v_proj"], kv_rep)])
-    g_sh, u_sh = rows_of(gate), rows_of(up)
-    lm = qmm.QuantizedWeight(*rows_of(draws["lm_head"]), "nvfp4")
+    kv_rep = tp_plan.placement("k_proj", world) == "replicated"
+    gdn_in = cat([col(nm, draws[nm]) for nm, _, _ in GDN_LINEARS[:4]])
+    attn_in = cat([col(nm, draws[nm]) for nm, _, _ in ATTN_LINEARS[:3]])
+    g_sh, u_sh = col("gate_proj", gate), col("up_proj", up)
+    tp_plan.mlp_slices(MLP_FFN, HIDDEN, "nvfp4", rank, world)   # SwiGLU rows == down's K-slice
+    lm = qmm.QuantizedWeight(*col("lm_head", draws["lm_head"]), "nvfp4")
     layers = []
     for li in range(64):
         attn = li % 4 == 3

@@ -124,3 +124,125 @@ def test_shard_range_rules():
             assert sum(rows) == 17408 and max(rows) - min(rows) <= 1
     with pytest.raises(qmm.QmmError):
         qmm.shard_range(5120, 17408 + 16, "nvfp4", 1, 0, 8)     # 17424 / 8 is not a whole group
+
+
+# ---- the decoder layer's placement (mlx-runner_b200/tp_plan.py) ------------
+
+SMALL_LAYER = {"in_proj_qkv": (160, 256), "in_proj_z": (96, 256), "in_proj_b": (8, 256), "in_proj_a": (8, 256),
+               "out_proj": (256, 192), "gate_proj": (512, 256), "up_proj": (512, 256), "down_proj": (256, 512)}
+
+
+def _layer(mode, seed=9):
+    import oracle
+    rng = np.random.default_rng(seed)
+    w = {nm: oracle.quantize((rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float32), mode)
+         for nm, shape in SMALL_LAYER.items()}
+    x = oracle.f32_to_bf16_bits(rng.standard_normal((3, 256), dtype=np.float32))
+    x6 = oracle.f32_to_bf16_bits(rng.standard_normal((3, 192), dtype=np.float32))
+    return w, x, x6
+
+
+def _silu_mul(g, u):
+    return g / (1.0 + np.exp(-g)) * u
+
+
+def _layer_worker(rank: int, world: int, port: int, mode: str, q):
+    try:
+        for p in (os.path.join(ROOT, "mlx-runner_b200"), os.path.join(ROOT, "oracle")):
+            sys.path.insert(0, p)
+        import torch
+        import torch.distributed as dist
+        import oracle
+        import qmm
+        import tp_plan
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        w, x, x6 = _layer(mode)
+        # in_proj: this rank's rows of qkv | z | b | a, concatenated (one launch
+        # on the GPU); the gathered blocks are reassembled per projection.
+        names = ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")
+        parts = [tp_plan.take(*w[nm], mode, nm, rank, world) for nm in names]
+        y_in = oracle.qmm_f64(x, np.concatenate([c for c, _ in parts]), np.concatenate([s for _, s in parts]), mode)
+        blocks = [None] * world
+        dist.all_gather_object(blocks, (y_in, [c.shape[0] for c, _ in parts]))
+        # MLP: gate / up rows of this rank -> SwiGLU -> down's K-slice -> sum.
+        s0, s1 = tp_plan.mlp_slices(512, 256, mode, rank, world)
+        g_c, g_s = tp_plan.take(*w["gate_proj"], mode, "gate_proj", rank, world)
+        u_c, u_s = tp_plan.take(*w["up_proj"], mode, "up_proj", rank, world)
+        assert g_c.shape[0] == s1 - s0 == u_c.shape[0]
+        h = _silu_mul(oracle.qmm_f64(x, g_c, g_s, mode), oracle.qmm_f64(x, u_c, u_s, mode))
+        d_c, d_s = tp_plan.take(*w["down_proj"], mode, "down_proj", rank, world)
+        part = torch.from_numpy(np.ascontiguousarray(h @ oracle.dequantize(d_c, d_s, mode).astype(np.float64).T))
+        dist.all_reduce(part)
+        # out_proj: this rank's K-slice of its input.
+        o_c, o_s = tp_plan.take(*w["out_proj"], mode, "out_proj", rank, world)
+        _, _, c0, cols = qmm.shard_range(256, 192, mode, 1, rank, world)
+        po = torch.from_numpy(np.ascontiguousarray(oracle.qmm_f64(np.ascontiguousarray(x6[:, c0:c0 + cols]),
+                                                                   o_c, o_s, mode)))
+        dist.all_reduce(po)
+        q.put((rank, blocks, h, part.numpy(), po.numpy(), (s0, s1)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:
+        q.put((rank, repr(exc), None, None, None, None))
+
+
+@pytest.mark.parametrize("mode", ["nvfp4", "mxfp8"])
+def test_tp_layer_plan_world2_gloo(mode):
+    """A decoder layer placed by tp_plan on two CPU ranks equals the unsharded
+    layer: column-parallel in_proj (concatenated per rank) reassembles exactly,
+    the SwiGLU rows of a rank are down_proj's K-slice there, and the
+    row-parallel sums (down, out_proj) match to fp64 summation order."""
+    import multiprocessing as mp
+    import oracle
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_layer_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        item = q.get(timeout=240)
+        res[item[0]] = item[1:]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, item in res.items():
+        assert not isinstance(item[0], str), f"rank {rank}: {item[0]}"
+
+    w, x, x6 = _layer(mode)
+    names = ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")
+    full = {nm: oracle.qmm_f64(x, *w[nm], mode) for nm in names}
+    g = oracle.qmm_f64(x, *w["gate_proj"], mode)
+    u = oracle.qmm_f64(x, *w["up_proj"], mode)
+    h_full = _silu_mul(g, u)
+    y_down = h_full @ oracle.dequantize(*w["down_proj"], mode).astype(np.float64).T
+    y_out = oracle.qmm_f64(x6, *w["out_proj"], mode)
+    for rank in range(world):
+        blocks, h, part, po, (s0, s1) = res[rank]
+        # Reassemble each projection from every rank's block of the concatenation.
+        for j, nm in enumerate(names):
+            pieces = []
+            for y_r, sizes in blocks:
+                off = sum(sizes[:j])
+                pieces.append(y_r[:, off:off + sizes[j]])
+            np.testing.assert_array_equal(np.concatenate(pieces, axis=1), full[nm])
+        np.testing.assert_array_equal(h, h_full[:, s0:s1])
+        np.testing.assert_allclose(part, y_down, rtol=1e-12, atol=1e-12 * np.abs(y_down).max())
+        np.testing.assert_allclose(po, y_out, rtol=1e-12, atol=1e-12 * np.abs(y_out).max())
+
+
+def test_tp_plan_placements():
+    import tp_plan
+    assert tp_plan.placement("in_proj_qkv", 2) == "column"
+    assert tp_plan.placement("down_proj", 8) == "row"
+    assert tp_plan.placement("k_proj", 4) == "column"      # 4 KV heads: one per rank
+    assert tp_plan.placement("k_proj", 8) == "replicated"  # more ranks than KV heads
+    assert tp_plan.placement("lm_head", 1) == "replicated"
+    with pytest.raises(KeyError):
+        tp_plan.placement("conv1d", 2)
+    for world in (2, 4, 8):                                 # config 5's FFN splits evenly
+        spans = [tp_plan.mlp_slices(17408, 5120, "nvfp4", r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == 17408
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
