@@ -116,14 +116,29 @@ void release_fused(qmm_comm* c) {
 // Collective (every rank calls it in the same order): allocates this rank's
 // receive buffer and flags, exchanges CUDA IPC handles with ncclAllGather,
 // maps the peers' buffers, and agrees (ncclAllReduce min) on whether every
-// rank succeeded.  Returns an error only for NCCL failures; a CUDA failure on
-// any rank leaves every rank on the NCCL path.
+// rank succeeded.  Returns an error for NCCL failures and when this rank
+// cannot hold the exchange's own scratch (then before any collective); a
+// failed buffer allocation or IPC mapping on any rank leaves every rank on the
+// NCCL path.
 int setup_fused(qmm_comm* c, int64_t cap) {
     const int P = c->nranks, me = c->rank;
     const char* env = std::getenv("QMM_TP_FUSED");
     if (P < 2 || P > qmm::kMaxTpRanks || cap <= 0 || (env && env[0] == '0')) return QMM_OK;
     cudaStream_t s = nullptr;
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return QMM_OK;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+        return qmm::set_error(QMM_ERR_CUDA, "setup of the fused exchange: cudaStreamCreate failed");
+    // The device buffers of the handle exchange ([P + 1] handle pairs, then the
+    // agreement flag).  Without them this rank cannot take part in the
+    // collectives below: it fails here, before any of them, and its peers wait
+    // in theirs until the caller's own timeout - as for a rank whose
+    // ncclCommInitRank failed.
+    const size_t hb = sizeof(cudaIpcMemHandle_t) * 2;
+    uint8_t* dbuf = nullptr;
+    if (cudaMalloc(&dbuf, hb * (P + 1) + sizeof(int)) != cudaSuccess) {
+        cudaStreamDestroy(s);
+        return qmm::set_error(QMM_ERR_OUT_OF_MEMORY, "setup of the fused exchange: cudaMalloc failed");
+    }
+    int* dok = reinterpret_cast<int*>(dbuf + hb * (P + 1));
     const int max_rb = (int)((cap + 127) / 128);
     int ok = 1;
     float* recv = nullptr;
@@ -138,24 +153,18 @@ int setup_fused(qmm_comm* c, int64_t cap) {
     std::memset(mine, 0, sizeof(mine));
     ok = ok && cudaIpcGetMemHandle(&mine[0], recv) == cudaSuccess;
     ok = ok && cudaIpcGetMemHandle(&mine[1], flags) == cudaSuccess;
-    // Exchange [P][2 handles] and the success flags.
-    const size_t hb = sizeof(mine);
-    uint8_t* dbuf = nullptr;
-    int* dok = nullptr;
+    // Exchange [P][2 handles] and the success flags: every rank takes part,
+    // whatever its own allocations gave (a failed one only sets ok = 0).
+    static_assert(sizeof(mine) == 2 * sizeof(cudaIpcMemHandle_t), "two handles per rank");
     int rc = QMM_OK;
-    if (cudaMalloc(&dbuf, hb * (P + 1)) != cudaSuccess || cudaMalloc(&dok, sizeof(int)) != cudaSuccess) {
-        ok = 0;  // still take part in the collectives below
-    }
     std::vector<uint8_t> all(hb * P);
-    if (dbuf && dok) {
-        cudaMemcpy(dbuf + hb * P, mine, hb, cudaMemcpyHostToDevice);
-        cudaMemcpy(dok, &ok, sizeof(int), cudaMemcpyHostToDevice);
-        if (ncclResult_t r = g_api.AllGather(dbuf + hb * P, dbuf, hb, ncclUint8, c->comm, s)) rc = nccl_fail(r, "ncclAllGather");
-        else if (ncclResult_t r2 = g_api.AllReduce(dok, dok, 1, ncclInt32, ncclMin, c->comm, s)) rc = nccl_fail(r2, "ncclAllReduce");
-        cudaStreamSynchronize(s);
-        cudaMemcpy(all.data(), dbuf, hb * P, cudaMemcpyDeviceToHost);
-        cudaMemcpy(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost);
-    }
+    cudaMemcpy(dbuf + hb * P, mine, hb, cudaMemcpyHostToDevice);
+    cudaMemcpy(dok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+    if (ncclResult_t r = g_api.AllGather(dbuf + hb * P, dbuf, hb, ncclUint8, c->comm, s)) rc = nccl_fail(r, "ncclAllGather");
+    else if (ncclResult_t r2 = g_api.AllReduce(dok, dok, 1, ncclInt32, ncclMin, c->comm, s)) rc = nccl_fail(r2, "ncclAllReduce");
+    cudaStreamSynchronize(s);
+    cudaMemcpy(all.data(), dbuf, hb * P, cudaMemcpyDeviceToHost);
+    cudaMemcpy(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost);
     c->ex.nranks = P;
     c->ex.rank = me;
     c->ex.max_rb = max_rb;
@@ -183,7 +192,6 @@ int setup_fused(qmm_comm* c, int64_t cap) {
         cudaMemcpy(&opened, dok, sizeof(int), cudaMemcpyDeviceToHost);
     }
     cudaFree(dbuf);
-    cudaFree(dok);
     cudaStreamDestroy(s);
     cudaGetLastError();   // a failed IPC call leaves a sticky-free error; it is handled by `ok`
     c->fused = ok && opened && rc == QMM_OK;
