@@ -418,13 +418,14 @@ int read_linear(const qmm_checkpoint* c, const char* prefix, std::vector<uint8_t
     if (w->dtype != QMM_DTYPE_U32 || w->shape.size() != 2 || s->dtype != QMM_DTYPE_U8 || s->shape.size() != 2 ||
         w->shape[0] != s->shape[0])
         return set_error(QMM_ERR_BAD_SHAPE, "'%s': expected U32 [N, P] codes and U8 [N, G] scales", prefix);
+    // Sizes first: the shape arithmetic below must not overflow on a hostile header.
+    if (shape_bytes(*w) < 0 || shape_bytes(*s) < 0 || w->shape[1] > INT64_MAX / 32 || s->shape[1] > INT64_MAX / 32)
+        return set_error(QMM_ERR_BAD_HEADER, "'%s': tensor sizes overflow", prefix);
     *n = w->shape[0];
     *k = w->shape[1] * 32 / c->spec.bits;
     if (s->shape[1] * c->spec.group_size != *k)
         return set_error(QMM_ERR_BAD_SHAPE, "'%s': %lld scale columns for k=%lld (group %d)", prefix,
                          (long long)s->shape[1], (long long)*k, c->spec.group_size);
-    if (shape_bytes(*w) < 0 || shape_bytes(*s) < 0)
-        return set_error(QMM_ERR_BAD_HEADER, "'%s': tensor sizes overflow", prefix);
     codes->resize((size_t)shape_bytes(*w));
     scales->resize((size_t)shape_bytes(*s));
     if (int rc = read_tensor(c, *w, codes->data())) return rc;

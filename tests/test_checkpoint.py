@@ -171,3 +171,22 @@ def test_inconsistent_quant_is_rejected_at_open(tmp_path):
     with pytest.raises(qmm.QmmError) as ei:
         qmm.Checkpoint(d)
     assert status(ei) == "InconsistentQuant"
+
+
+def test_hostile_linear_shapes_fail_before_any_upload(tmp_path):
+    """A header whose linear is absurdly large (2^60 packed columns) parses, and
+    loading it fails with BadHeader on the host - the shape arithmetic is
+    checked before it runs and nothing reaches the device."""
+    d = str(tmp_path)
+    hdr = {"big.weight": {"dtype": "U32", "shape": [1, 2 ** 60], "data_offsets": [0, 8]},
+           "big.scales": {"dtype": "U8", "shape": [1, 2 ** 59], "data_offsets": [8, 16]}}
+    write_shard(os.path.join(d, "s.safetensors"), json.dumps(hdr), bytes(16))
+    write_index(d, {"big.weight": "s.safetensors", "big.scales": "s.safetensors"})
+    ck = qmm.Checkpoint(d)
+    assert ck.spec.astuple() == ("nvfp4", 16, 4)          # r = 2^60 / 2^59 = 2
+    import ctypes
+    h = ctypes.c_void_p()
+    rc = qmm.lib().qmm_checkpoint_load_linear(ck._h, b"big", None, ctypes.byref(h))
+    assert qmm.STATUS_NAMES.get(rc) == "BadHeader" and not h.value
+    qmm.take_error()
+    ck.close()
