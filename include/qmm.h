@@ -316,6 +316,17 @@ int qmm_tp_unique_id(void* id128);
 int qmm_tp_comm_create(const void* id128, int nranks, int rank, int64_t max_partial_elems,
                        qmm_comm** out);
 int qmm_tp_comm_destroy(qmm_comm* c);
+/* Test hook, no reference counterpart (beside the fault hooks of
+ * src/mlx.zig:562-595): a communicator of `nranks` ranks (2..8) in which this
+ * process is `rank` and the other ranks never run - their receive buffers and
+ * flags are local allocations that nothing else writes, and no NCCL is used.
+ * qmm_tp_run_rowparallel on it takes the fused decode exchange (M <= 8, a
+ * resident weight with decode state, 16-byte aligned x rows; anything else is
+ * QMM_ERR_BAD_ARGUMENT), pushes its partial sums, waits the bounded 2 s for the
+ * absent ranks, gives up and writes y from what it has; qmm_device_status then
+ * reports QMM_ERR_TIMEOUT.  This exercises the device-side failure path on one
+ * GPU without a fault or a hang. */
+int qmm_tp_comm_create_detached(int nranks, int rank, int64_t max_partial_elems, qmm_comm** out);
 
 /* In-place bf16 sum all-reduce of `count` elements on `stream`. */
 int qmm_tp_allreduce_bf16(qmm_comm* c, void* buf_dev, int64_t count, void* stream);

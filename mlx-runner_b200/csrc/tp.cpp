@@ -49,6 +49,9 @@ struct qmm_comm {
     // Fused row-parallel exchange (peer receive buffers mapped over CUDA IPC).
     bool fused = false;
     qmm::TpExchange ex;
+    // qmm_tp_comm_create_detached: no NCCL, the other ranks' buffers are local
+    // allocations that nothing else writes.
+    bool detached = false;
 };
 
 namespace {
@@ -101,6 +104,11 @@ int nccl_fail(ncclResult_t r, const char* what) {
 void release_fused(qmm_comm* c) {
     for (int r = 0; r < c->nranks && r < qmm::kMaxTpRanks; ++r) {
         if (r == c->rank) continue;
+        if (c->detached) {
+            cudaFree(c->ex.recv[r]);
+            cudaFree(c->ex.flags[r]);
+            continue;
+        }
         if (c->ex.recv[r]) cudaIpcCloseMemHandle(c->ex.recv[r]);
         if (c->ex.flags[r]) cudaIpcCloseMemHandle(c->ex.flags[r]);
     }
@@ -255,6 +263,51 @@ extern "C" int qmm_tp_comm_create(const void* id128, int nranks, int rank, int64
     return QMM_OK;
 }
 
+extern "C" int qmm_tp_comm_create_detached(int nranks, int rank, int64_t max_partial_elems, qmm_comm** out) {
+    if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_comm_create_detached: injected failure");
+    if (!out) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    if (nranks < 2 || nranks > qmm::kMaxTpRanks || rank < 0 || rank >= nranks || max_partial_elems <= 0)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "rank %d of %d (2..%d ranks), capacity %lld", rank, nranks,
+                         qmm::kMaxTpRanks, (long long)max_partial_elems);
+    qmm_comm* c = new qmm_comm();
+    c->nranks = nranks;
+    c->rank = rank;
+    c->detached = true;
+    c->capacity = max_partial_elems;
+    if (cudaError_t e = cudaGetDevice(&c->device)) {
+        delete c;
+        return qmm::cuda_error(e, "cudaGetDevice");
+    }
+    // The same buffers setup_fused gives every rank, all on this device.
+    const int P = nranks;
+    const int64_t cap = max_partial_elems;
+    const int max_rb = (int)((cap + 127) / 128);
+    const size_t recv_bytes = (size_t)2 * P * cap * sizeof(float), flag_bytes = (size_t)P * max_rb * sizeof(unsigned int);
+    cudaError_t e = cudaSuccess;
+    for (int r = 0; r < P && e == cudaSuccess; ++r) {
+        if ((e = cudaMalloc(&c->ex.recv[r], recv_bytes)) == cudaSuccess &&
+            (e = cudaMemset(c->ex.recv[r], 0, recv_bytes)) == cudaSuccess &&
+            (e = cudaMalloc(&c->ex.flags[r], flag_bytes)) == cudaSuccess)
+            e = cudaMemset(c->ex.flags[r], 0, flag_bytes);
+    }
+    if (e == cudaSuccess && (e = cudaMalloc(&c->ex.gen, (size_t)max_rb * sizeof(unsigned int))) == cudaSuccess)
+        e = cudaMemset(c->ex.gen, 0, (size_t)max_rb * sizeof(unsigned int));
+    c->ex.nranks = P;
+    c->ex.rank = rank;
+    c->ex.max_rb = max_rb;
+    c->ex.cap = cap;
+    if (e != cudaSuccess) {
+        const int rc = qmm::cuda_error(e, "qmm_tp_comm_create_detached");
+        release_fused(c);
+        delete c;
+        return rc;
+    }
+    c->fused = true;
+    *out = c;
+    return QMM_OK;
+}
+
 extern "C" int qmm_tp_comm_destroy(qmm_comm* c) {
     if (!c) return QMM_OK;
     int rc = QMM_OK;
@@ -270,6 +323,7 @@ extern "C" int qmm_tp_comm_destroy(qmm_comm* c) {
 extern "C" int qmm_tp_allreduce_bf16(qmm_comm* c, void* buf_dev, int64_t count, void* stream) {
     if (qmm::fault_hit()) return set_error(QMM_ERR_INJECTED, "qmm_tp_allreduce_bf16: injected failure");
     if (!c) return set_error(QMM_ERR_BAD_ARGUMENT, "comm is NULL");
+    if (c->detached) return set_error(QMM_ERR_BAD_ARGUMENT, "a detached communicator has no collectives");
     if (count < 0 || (count > 0 && !buf_dev)) return set_error(QMM_ERR_BAD_ARGUMENT, "bad buffer");
     if (ncclResult_t r = g_api.AllReduce(buf_dev, buf_dev, (size_t)count, ncclBfloat16, ncclSum, c->comm,
                                          static_cast<cudaStream_t>(stream)))
@@ -296,6 +350,9 @@ extern "C" int qmm_tp_run_rowparallel(const qmm_weight* w, qmm_comm* c, const vo
         if (int rc = qmm::run_rowparallel_fused(w, &c->ex, x_dev, m, ldx, y_dev, ldy, s, &handled)) return rc;
         if (handled) return QMM_OK;
     }
+    if (c->detached)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "a detached communicator runs only the fused decode exchange "
+                                               "(M <= 8, a resident decode weight, 16-byte aligned x rows)");
     if (int rc = qmm::run_partial_f32(w, x_dev, m, ldx, c->partial, n, s)) return rc;
     if (ncclResult_t r = g_api.AllReduce(c->partial, c->partial, (size_t)(m * n), ncclFloat32, ncclSum, c->comm, s))
         return nccl_fail(r, "ncclAllReduce(f32)");

@@ -48,7 +48,8 @@ EXPORTS = (
     "qmm_swiglu_weight_create", "qmm_swiglu_run", "qmm_lm_head_argmax",
     "qmm_checkpoint_open", "qmm_checkpoint_close", "qmm_checkpoint_spec", "qmm_checkpoint_tensors",
     "qmm_checkpoint_read", "qmm_checkpoint_load_linear", "qmm_checkpoint_load_swiglu",
-    "qmm_tp_comm_create", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16", "qmm_tp_run_rowparallel",
+    "qmm_tp_comm_create", "qmm_tp_comm_create_detached", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16",
+    "qmm_tp_run_rowparallel",
     "qmm_last_error", "qmm_error_pending", "qmm_device_status", "qmm_fault_arm", "qmm_fault_fired",
 )
 
@@ -131,6 +132,7 @@ def lib() -> ctypes.CDLL:
     L.qmm_tp_unique_id.argtypes = [vp]
     L.qmm_tp_comm_create.argtypes = [vp, i32, i32, i64, ctypes.POINTER(vp)]
     L.qmm_tp_comm_destroy.argtypes = [vp]
+    L.qmm_tp_comm_create_detached.argtypes = [i32, i32, i64, ctypes.POINTER(vp)]
     L.qmm_tp_allreduce_bf16.argtypes = [vp, vp, i64, vp]
     L.qmm_tp_run_rowparallel.argtypes = [vp, vp, vp, i64, i64, vp, i64, vp]
     L.qmm_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
@@ -540,6 +542,17 @@ class TPComm:
         buf = ctypes.create_string_buffer(128)
         check(lib().qmm_tp_unique_id(buf))
         return buf.raw
+
+    @classmethod
+    def detached(cls, nranks: int, rank: int, max_partial_elems: int) -> "TPComm":
+        """Test hook: a communicator whose other ranks never run (no NCCL); the
+        fused exchange on it times out and qmm_device_status reports Timeout."""
+        obj = cls.__new__(cls)
+        h = ctypes.c_void_p()
+        check(lib().qmm_tp_comm_create_detached(nranks, rank, max_partial_elems, ctypes.byref(h)))
+        obj._h = h
+        obj.nranks, obj.rank = nranks, rank
+        return obj
 
     def run_rowparallel(self, weight: QuantizedWeight, x_shard, out=None, stream=None):
         torch = _torch()

@@ -170,3 +170,15 @@ def test_quantize_validates_on_host():
     assert call(w=None) == "BadArgument"
     assert call(c=ctypes.c_void_p(18)) == "BadArgument"  # codes not 4-byte aligned
     assert call(n=0) == 0                                # empty: nothing to do
+
+
+def test_detached_comm_validates_on_host():
+    L = qmm.lib()
+    h = ctypes.c_void_p()
+    qmm.take_error()
+    assert _status(L.qmm_tp_comm_create_detached(1, 0, 64, ctypes.byref(h))) == "BadArgument"   # < 2 ranks
+    assert _status(L.qmm_tp_comm_create_detached(9, 0, 64, ctypes.byref(h))) == "BadArgument"   # > 8 ranks
+    assert _status(L.qmm_tp_comm_create_detached(2, 2, 64, ctypes.byref(h))) == "BadArgument"   # rank out of range
+    assert _status(L.qmm_tp_comm_create_detached(2, 0, 0, ctypes.byref(h))) == "BadArgument"    # no capacity
+    assert _status(L.qmm_tp_comm_create_detached(2, 0, 64, None)) == "BadArgument"
+    assert not h.value

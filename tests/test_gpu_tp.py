@@ -1,7 +1,7 @@
 """Tensor parallelism on 2 GPUs (one process per GPU): K-sharded row-parallel
-GEMM with the fp32 NCCL all-reduce, and N-sharded column-parallel shards
-(no collective), both checked against the CPU oracle.  Skipped with fewer
-than 2 GPUs.
+GEMM with the cross-rank sum, and N-sharded column-parallel shards
+(no collective), both checked against the CPU oracle; skipped with fewer
+than 2 GPUs.  On one GPU: the exchange's bounded wait running out.
 """
 import os
 import sys
@@ -85,3 +85,36 @@ def test_tp_two_gpus(mode, n, k, m):
         assert oracle.parity_violations(y, ref, absref) == 0
     y_n = np.concatenate([oracle.bf16_bits_to_f32(out[r][1]) for r in range(world)], axis=1)
     assert oracle.parity_violations(y_n, ref, absref) == 0
+
+
+def test_exchange_wait_times_out_and_reports(cuda_device):
+    """The fused row-parallel exchange waiting for ranks that never run (a
+    detached communicator: their flags are local memory nothing writes) gives
+    up after its bounded 2 s wait; qmm_device_status reports Timeout once, and
+    the device stays usable - a plain decode afterwards meets the parity bar.
+    One GPU; no fault, no hang."""
+    import time
+    import torch
+    import oracle
+    import qmm
+    n, k, m = 256, 2048, 2
+    codes, scales, x = _case("nvfp4", n, k, m, seed=4)
+    xt = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16)
+    comm = qmm.TPComm.detached(2, 0, m * n)
+    w = qmm.QuantizedWeight(codes, scales, "nvfp4", shard=(1, 0, 2))
+    xs = xt[:, :k // 2].contiguous().to(cuda_device)
+    t0 = time.monotonic()
+    comm.run_rowparallel(w, xs)
+    with pytest.raises(qmm.QmmError) as ei:
+        qmm.device_status()
+    assert ei.value.name == "Timeout"
+    assert time.monotonic() - t0 < 60
+    qmm.device_status()                       # the word was cleared
+    w.close()
+    comm.close()
+    w2 = qmm.QuantizedWeight(codes, scales, "nvfp4")
+    y = w2(xt.to(cuda_device)).cpu().view(torch.int16).numpy().view(np.uint16)
+    w2.close()
+    got = oracle.bf16_bits_to_f32(y)
+    assert oracle.parity_violations(got, oracle.qmm_f64(x, codes, scales, "nvfp4"),
+                                    oracle.abs_qmm_f64(x, codes, scales, "nvfp4")) == 0
