@@ -1,6 +1,6 @@
 """Benchmark of the quantized-matmul hot path (one JSON line on rank 0).
 
-Headline workload (the config the metric is quoted on):
+Headline workload (benchmark config 2, the config the metric is quoted on):
 nvfp4 small-batch GEMM for decode + MTP verify, x bf16 [M, 17408] with
 M = 1, 2, 3, 4, W [5120, 17408] nvfp4 (E2M1 codes, group 16, UE4M3 scales).
 On N GPUs the weight is K-sharded (row-parallel): every rank multiplies its
@@ -185,7 +185,7 @@ CONFIG = {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], 
           "mode": MODE, "m": list(M_SET), "n": N_OUT, "k": K_IN}
 
 
-PREFILL = {"m": 32768, "n": 34816, "k": 5120, "mode": "nvfp4"}
+PREFILL = {"m": 32768, "n": 34816, "k": 5120, "mode": "nvfp4"}   # benchmark config 3
 
 
 def _quantized_normal(qmm, n: int, k: int, mode: str, dev, seed: int):
@@ -200,7 +200,7 @@ def _quantized_normal(qmm, n: int, k: int, mode: str, dev, seed: int):
 
 
 def prefill_measure(args, qmm, dev, world: int, rank: int, barrier, max_over_ranks) -> dict:
-    """BASELINE config 3 (32k-token nvfp4 gate/up GEMM) on the tcgen05 kernel;
+    """Benchmark config 3 (32k-token nvfp4 gate/up GEMM) on the tcgen05 kernel;
     N-sharded (column-parallel, no collective) over the GPUs."""
     import torch
     m, n, k, mode = args.prefill_m, PREFILL["n"], PREFILL["k"], PREFILL["mode"]
@@ -409,19 +409,19 @@ def next_rows_measure(args, qmm, dev) -> dict:
     return out
 
 
-# the linear stack of one decode step of a 64-layer
+# Benchmark config 5: the linear stack of one decode step of a 64-layer
 # hybrid (hidden 5120, FFN 17408, vocab 248320), nvfp4, M = 3 (MTP verify).
 GDN_LINEARS = (("in_proj_qkv", 10240, 5120), ("in_proj_z", 6144, 5120), ("in_proj_b", 48, 5120),
                ("in_proj_a", 48, 5120), ("out_proj", 5120, 6144))
 ATTN_LINEARS = (("q_proj", 12288, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120), ("o_proj", 5120, 6144))
 MLP_FFN, HIDDEN, VOCAB = 17408, 5120, 248320
-# the prefill GEMMs of one GDN layer, mxfp8, T = 32768.
+# Benchmark config 4: the prefill GEMMs of one GDN layer, mxfp8, T = 32768.
 GDN_PREFILL = (("in_proj_qkvz", 16384, 5120), ("in_proj_ba", 96, 5120), ("out_proj", 5120, 6144),
                ("gate_up", 34816, 5120), ("down", 5120, 17408))
 
 
 def configs_measure(args, qmm, dev) -> dict:
-    """BASELINE configs 1, 4 and 5 on one GPU, each through the C-ABI calls,
+    """Benchmark configs 1, 4 and 5 on one GPU, each through the C-ABI calls,
     with weights ~N(0, 0.02^2) quantized on the GPU by qmm_quantize:
       cfg1  mxfp8 GEMV x [1, 5120] . W[17408, 5120]^T; weight copies rotate
             (inputs larger than L2), CUDA-graph replays;
@@ -585,7 +585,7 @@ def configs_measure(args, qmm, dev) -> dict:
 
 
 def cfg5_tp_measure(qmm, dev, world: int, rank: int, comm, barrier, max_over_ranks, sum_over_ranks) -> dict:
-    """BASELINE config 5 tensor-parallel over `world` GPUs, one rank each:
+    """Benchmark config 5 tensor-parallel over `world` GPUs, one rank each:
     column-parallel in_proj (qkv|z|b|a), q|k|v, gate / up (SwiGLU) and
     lm_head - each rank holds its rows of every tensor, no collective;
     row-parallel out_proj, o_proj and down - each rank holds a K-slice and

@@ -1,5 +1,5 @@
 """bench.py on the CPU: the algorithmic bytes and FLOPs its roofline fractions
-divide by are the workload's own figures (codes +
+divide by are the workload's own figures (benchmark configs 1-5: codes +
 scales + x + y per call, 2*M*N*K per call, the config 5 stack's 25.6 G
 weight elements), and the reference arm prints the contract's JSON line.
 No GPU is used: the reference arm times the CPU restatement."""

@@ -2,7 +2,7 @@
 
 Same bar as the GEMV tests: within 1 bf16 ulp (+ 2^-20 * sum|x||w|) of the
 fp64 dequantise-then-matmul per element; relative Frobenius <= 2e-3 at the
-BASELINE config sizes.  Full-size configs are checked on sampled rows (every
+benchmark config sizes.  Full-size configs are checked on sampled rows (every
 tile row position is covered by the sample) plus a full-tensor comparison
 against torch's bf16 matmul over our exact bf16 dequantisation.
 """
@@ -97,7 +97,7 @@ def _torch_check(y, x, w, tol=2e-3):
     ("cfg3 gate/up", "nvfp4", 2048, 34816, 5120),
 ])
 def test_config_shapes_sampled(cuda_device, name, mode, m, n, k):
-    """BASELINE configs 3/4 weight shapes at a 2048-token chunk (the
+    """Benchmark configs 3/4 weight shapes at a 2048-token chunk (the
     reference's prefill chunk), sampled rows against the fp64 oracle."""
     codes, scales = make_weight(n, k, mode, seed=n)
     x = make_x(m, k, seed=n).to(cuda_device)
@@ -110,7 +110,7 @@ def test_config_shapes_sampled(cuda_device, name, mode, m, n, k):
 
 
 def test_cfg3_full_32k_prefill(cuda_device):
-    """BASELINE config 3 at full size: x [32768, 5120], W [34816, 5120] nvfp4."""
+    """Benchmark config 3 at full size: x [32768, 5120], W [34816, 5120] nvfp4."""
     m, n, k = 32768, 34816, 5120
     codes, scales = make_weight(n, k, "nvfp4", seed=0)
     x = make_x(m, k, seed=0).to(cuda_device)

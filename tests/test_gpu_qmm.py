@@ -2,7 +2,7 @@
 
 Bar: dequantisation bit-exact; qmm outputs within 1 bf16 ulp (plus an fp32
 accumulation allowance of 2^-20 * sum|x||w|) of the fp64 dequantise-then-
-matmul per element, and relative Frobenius error <= 2e-3 at the BASELINE
+matmul per element, and relative Frobenius error <= 2e-3 at the benchmark
 config sizes (the north_star tolerance; bf16 output rounding alone costs
 ~1.6e-3).
 """
@@ -163,7 +163,7 @@ def test_stateless_matches_handle_and_strides(cuda_device, mode):
 
 
 def test_config1_mxfp8_gemv_full(cuda_device):
-    """x [1, 5120], W [17408, 5120] mxfp8."""
+    """Benchmark config 1: x [1, 5120], W [17408, 5120] mxfp8."""
     codes, scales = make_weight(17408, 5120, "mxfp8", seed=0)
     x = make_x(1, 5120, seed=0).to(cuda_device)
     rf = check_parity(qmm.QuantizedWeight(codes, scales, "mxfp8")(x), x, codes, scales, "mxfp8", frob=2e-3)
@@ -172,7 +172,7 @@ def test_config1_mxfp8_gemv_full(cuda_device):
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4])
 def test_config2_nvfp4_small_batch_full(cuda_device, m):
-    """x [M, 17408], W [5120, 17408] nvfp4, M = 1..4."""
+    """Benchmark config 2: x [M, 17408], W [5120, 17408] nvfp4, M = 1..4."""
     codes, scales = make_weight(5120, 17408, "nvfp4", seed=0)
     x = make_x(m, 17408, seed=m).to(cuda_device)
     check_parity(qmm.QuantizedWeight(codes, scales, "nvfp4")(x), x, codes, scales, "nvfp4", frob=2e-3)

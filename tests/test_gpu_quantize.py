@@ -1,6 +1,6 @@
 """qmm_quantize (src/mlx.zig:278 mlx_quantize, as src/model.zig:1577 calls
 it) on the GPU against the oracle's quantizer, byte for byte: the hard cases
-(ties, saturation, subnormals, NaN / inf / zero groups)
+(ties, saturation, subnormals, NaN / inf / zero groups), benchmark configs 1
 and 2 at full size, bf16 input, strided and unaligned rows; then the
 reference's own qmm test (src/model.zig:1561-1609) through quantize ->
 quantized_matmul -> dequantize."""
@@ -38,7 +38,7 @@ def test_quantize_hard_cases(cuda_device, mode):
 
 @pytest.mark.parametrize("mode,n,k", [("mxfp8", 17408, 5120), ("nvfp4", 5120, 17408)])
 def test_quantize_config_shapes(cuda_device, mode, n, k):
-    """BASELINE configs 1 and 2: W ~ N(0, 0.02^2) [N, K], seed 0."""
+    """Benchmark configs 1 and 2: W ~ N(0, 0.02^2) [N, K], seed 0."""
     rng = np.random.default_rng(0)
     w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
     c, s = gpu_quantize(w, mode, cuda_device)

@@ -68,7 +68,7 @@ def test_swiglu_decode_small(cuda_device, mode, m):
 
 @pytest.mark.parametrize("m", [1, 3])
 def test_swiglu_decode_model_shape(cuda_device, m):
-    """The model's gate / up pair: [17408, 5120] each, nvfp4 (BASELINE config 3's
+    """The model's gate / up pair: [17408, 5120] each, nvfp4 (benchmark config 3's
     fused weight [34816, 5120] is their concatenation)."""
     n, k, mode = 17408, 5120, "nvfp4"
     gate, up = make_weight(n, k, mode, seed=1), make_weight(n, k, mode, seed=2)

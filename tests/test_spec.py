@@ -31,7 +31,7 @@ def _err(tensors):
 
 
 def test_config_shapes():
-    # mxfp8 [17408, 5120] and nvfp4 [5120, 17408].
+    # benchmark configs: mxfp8 [17408, 5120] and nvfp4 [5120, 17408].
     assert qmm.infer_quant_spec([("a.weight", "U32", [17408, 1280]), ("a.scales", "U8", [17408, 160])]) == \
         ("mxfp8", 32, 8)
     assert qmm.infer_quant_spec([("a.weight", "U32", [5120, 2176]), ("a.scales", "U8", [5120, 1088])]) == \
