@@ -30,15 +30,15 @@ def test_library_exports_every_declared_symbol():
     assert L.qmm_abi_version() == 1
 
 
-def _mm(**kw):
-    """qmm_quantized_matmul with harmless defaults (never reaches the device)."""
+def _mm(entry="qmm_quantized_matmul", **kw):
+    """qmm_quantized_matmul (or its no-alloc twin, same arguments) with harmless
+    defaults (never reaches the device)."""
     a = dict(y=1 << 20, ldy=8, x=1 << 20, m=1, k=32, ldx=32, w=1 << 20, w_rows=8, w_cols=8,
              s=1 << 20, s_rows=8, s_cols=1, biases=None, transpose=True, group=None, bits=None, mode=b"mxfp8")
     a.update(kw)
-    return qmm.lib().qmm_quantized_matmul(a["y"], a["ldy"], a["x"], a["m"], a["k"], a["ldx"], a["w"], a["w_rows"],
-                                          a["w_cols"], a["s"], a["s_rows"], a["s_cols"], a["biases"], a["transpose"],
-                                          qmm.OptionalInt.of(a["group"]), qmm.OptionalInt.of(a["bits"]), a["mode"],
-                                          None)
+    return getattr(qmm.lib(), entry)(a["y"], a["ldy"], a["x"], a["m"], a["k"], a["ldx"], a["w"], a["w_rows"],
+                                     a["w_cols"], a["s"], a["s_rows"], a["s_cols"], a["biases"], a["transpose"],
+                                     qmm.OptionalInt.of(a["group"]), qmm.OptionalInt.of(a["bits"]), a["mode"], None)
 
 
 def _status(rc):
@@ -46,29 +46,33 @@ def _status(rc):
     return qmm.STATUS_NAMES.get(rc, rc)
 
 
-def test_validation_before_any_device_work():
+@pytest.mark.parametrize("entry", ["qmm_quantized_matmul", "qmm_quantized_matmul_noalloc"])
+def test_validation_before_any_device_work(entry):
+    import functools
+    _mm_ = functools.partial(_mm, entry)
     qmm.take_error()
-    assert _status(_mm(mode=b"affine")) == "BadMode"
-    assert _status(_mm(group=64)) == "BadMode"
-    assert _status(_mm(biases=1 << 20)) == "BadArgument"
-    assert _status(_mm(transpose=False)) == "BadArgument"
-    assert _status(_mm(k=48)) == "BadShape"                       # not a multiple of group 32
-    assert _status(_mm(w_cols=4)) == "BadShape"                   # packs 16, not k = 32
-    assert _status(_mm(s_cols=2)) == "BadShape"                   # 2 groups for k = 32
-    assert _status(_mm(s_rows=7)) == "BadShape"
-    assert _status(_mm(ldx=16)) == "BadShape"
-    assert _status(_mm(ldy=4)) == "BadShape"
-    assert _status(_mm(x=None)) == "BadArgument"
-    assert _status(_mm(x=(1 << 20) + 2)) == "BadArgument"         # x not 4-byte aligned
-    assert _status(_mm(m=-1)) == "BadShape"
+    assert _status(_mm_(mode=b"affine")) == "BadMode"
+    assert _status(_mm_(group=64)) == "BadMode"
+    assert _status(_mm_(biases=1 << 20)) == "BadArgument"
+    assert _status(_mm_(transpose=False)) == "BadArgument"
+    assert _status(_mm_(k=48)) == "BadShape"                       # not a multiple of group 32
+    assert _status(_mm_(w_cols=4)) == "BadShape"                   # packs 16, not k = 32
+    assert _status(_mm_(s_cols=2)) == "BadShape"                   # 2 groups for k = 32
+    assert _status(_mm_(s_rows=7)) == "BadShape"
+    assert _status(_mm_(ldx=16)) == "BadShape"
+    assert _status(_mm_(ldy=4)) == "BadShape"
+    assert _status(_mm_(x=None)) == "BadArgument"
+    assert _status(_mm_(x=(1 << 20) + 2)) == "BadArgument"         # x not 4-byte aligned
+    assert _status(_mm_(m=-1)) == "BadShape"
     # nvfp4: k = 16 is valid (one group), w packs 8 codes per word
-    assert _status(_mm(mode=b"nvfp4", k=16, ldx=16, w_cols=2, s_cols=1, ldy=4)) == "BadShape"  # ldy < n = 8
+    assert _status(_mm_(mode=b"nvfp4", k=16, ldx=16, w_cols=2, s_cols=1, ldy=4)) == "BadShape"  # ldy < n = 8
 
 
-def test_empty_inputs_are_noops():
+@pytest.mark.parametrize("entry", ["qmm_quantized_matmul", "qmm_quantized_matmul_noalloc"])
+def test_empty_inputs_are_noops(entry):
     # m == 0 or n == 0 returns OK without touching the device (or its pointers).
-    assert _mm(m=0, x=None, y=None) == 0
-    assert _mm(w_rows=0, s_rows=0, w=None, s=None) == 0
+    assert _mm(entry, m=0, x=None, y=None) == 0
+    assert _mm(entry, w_rows=0, s_rows=0, w=None, s=None) == 0
 
 
 def test_error_latch_first_wins_and_clears():
