@@ -59,6 +59,21 @@ def test_dequantize_bit_exact(cuda_device, mode, n, k):
     np.testing.assert_array_equal(got16, oracle.f32_to_bf16_bits(ref))
 
 
+@pytest.mark.parametrize("mode,n,k", [("mxfp8", 17408, 5120), ("nvfp4", 5120, 17408), ("nvfp4", 34816, 5120),
+                                      ("mxfp8", 16384, 5120), ("mxfp8", 96, 5120), ("mxfp8", 5120, 6144),
+                                      ("mxfp8", 5120, 17408)])
+def test_dequantize_config_shapes(cuda_device, mode, n, k):
+    """Seeded W at every benchmark weight shape (configs 1-4) at full size:
+    the GPU dequantisation equals the oracle's bit for bit."""
+    import torch
+    codes, scales = make_weight(n, k, mode, seed=7)
+    w = qmm.QuantizedWeight(codes, scales, mode)
+    got = w.dequantize(torch.float32).cpu().numpy()
+    w.close()
+    ref = oracle.dequantize(codes, scales, mode)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
 def test_dequantize_every_code(cuda_device):
     """All 256 E4M3 codes under several UE8M0 scales, all 16 E2M1 codes under
     all 127 non-negative finite UE4M3 scales: exact against the oracle."""
