@@ -235,6 +235,34 @@ def _as_2d(x):
     return x2
 
 
+def _need_cuda(name: str, t, device: Optional[int] = None) -> None:
+    """Raise unless t is a CUDA tensor (on `device` when given): the library
+    hands data_ptr() to kernels, and a host or another GPU's pointer there
+    would fault the device instead of failing the call."""
+    if not getattr(t, "is_cuda", False):
+        raise QmmError(7, f"{name} must be a CUDA tensor (got {getattr(t, 'device', type(t).__name__)})")
+    if device is not None and t.device.index != device:
+        raise QmmError(7, f"{name} is on cuda:{t.device.index}, the weight on cuda:{device}")
+
+
+def _check_out(out, rows: int, cols: int, device: Optional[int] = None) -> None:
+    """A caller's output buffer must hold [rows, cols] bf16 with unit column
+    stride: the library sees only its row stride, not its size."""
+    torch = _torch()
+    _need_cuda("out", out, device)
+    if out.dtype != torch.bfloat16 or out.dim() != 2 or out.stride(1) != 1 or out.shape[0] < rows \
+            or out.shape[1] < cols:
+        raise QmmError(7, f"out must be bfloat16 [>= {rows}, >= {cols}] with unit column stride, "
+                          f"got {tuple(out.shape)} {out.dtype}")
+
+
+def _need_packed(w, scales) -> None:
+    _need_cuda("w", w)
+    _need_cuda("scales", scales, w.device.index)
+    if w.dim() != 2 or scales.dim() != 2 or not w.is_contiguous() or not scales.is_contiguous():
+        raise QmmError(7, "w and scales must be contiguous 2-D tensors (the checkpoint layout)")
+
+
 def quantized_matmul(x, w, scales, biases=None, transpose: bool = True, group_size: Optional[int] = None,
                      bits: Optional[int] = None, mode: str = "mxfp8", stream=None, out=None):
     """y = x . dequant(w, scales)^T for x bf16 [..., K] on the GPU.
@@ -245,9 +273,13 @@ def quantized_matmul(x, w, scales, biases=None, transpose: bool = True, group_si
     torch = _torch()
     if x.dtype != torch.bfloat16:
         raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+    _need_packed(w, scales)
+    _need_cuda("x", x, w.device.index)
     x2 = _as_2d(x)
     n = w.shape[0]
     m, k = x2.shape
+    if out is not None:
+        _check_out(out, m, n, w.device.index)
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     check(lib().qmm_quantized_matmul(
         y.data_ptr(), y.stride(0), x2.data_ptr(), m, k, x2.stride(0),
@@ -266,8 +298,11 @@ def quantized_matmul_noalloc(x, w, scales, out, biases=None, transpose: bool = T
     torch = _torch()
     if x.dtype != torch.bfloat16:
         raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+    _need_packed(w, scales)
+    _need_cuda("x", x, w.device.index)
     x2 = _as_2d(x)
     m, k = x2.shape
+    _check_out(out, m, w.shape[0], w.device.index)
     check(lib().qmm_quantized_matmul_noalloc(
         out.data_ptr(), out.stride(0), x2.data_ptr(), m, k, x2.stride(0),
         w.data_ptr(), w.shape[0], w.shape[1], scales.data_ptr(), scales.shape[0], scales.shape[1],
@@ -291,6 +326,7 @@ def quantize(w, mode: str = "mxfp8", group_size: Optional[int] = None, bits: Opt
         raise QmmError(5, f"quantize input must be float32 or bfloat16, got {w.dtype}")
     if w.dim() != 2:
         raise QmmError(1, f"quantize takes a 2-D weight, got shape {tuple(w.shape)}")
+    _need_cuda("w", w)
     if w.stride(1) != 1:
         w = w.contiguous()
     spec = spec_from_args(group_size, bits, mode)
@@ -363,8 +399,11 @@ class QuantizedWeight:
         torch = _torch()
         if x.dtype != torch.bfloat16:
             raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        _need_cuda("x", x, self.device)
         x2 = _as_2d(x)
         m = x2.shape[0]
+        if out is not None:
+            _check_out(out, m, self.n, self.device)
         y = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
         check(lib().qmm_run(self.handle, x2.data_ptr(), m, x2.stride(0), y.data_ptr(), y.stride(0), True,
                             _stream_handle(stream)))
@@ -376,6 +415,7 @@ class QuantizedWeight:
         torch = _torch()
         if x.dtype != torch.bfloat16:
             raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        _need_cuda("x", x, self.device)
         x2 = _as_2d(x)
         m = x2.shape[0]
         ids = torch.empty((m,), dtype=torch.int32, device=x.device)
@@ -431,8 +471,11 @@ class SwiGLUWeight(QuantizedWeight):
         torch = _torch()
         if x.dtype != torch.bfloat16:
             raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        _need_cuda("x", x, self.device)
         x2 = _as_2d(x)
         m = x2.shape[0]
+        if out is not None:
+            _check_out(out, m, self.n, self.device)
         h = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
         check(lib().qmm_swiglu_run(self.handle, x2.data_ptr(), m, x2.stride(0), h.data_ptr(), h.stride(0),
                                    _stream_handle(stream)))
@@ -449,6 +492,11 @@ def linear(weight: Optional[QuantizedWeight], x, has_packed_u32: bool = True, ou
     if weight is None:
         check(lib().qmm_linear(None, has_packed_u32, x2.data_ptr(), x2.shape[0], x2.stride(0), None, 0,
                                _stream_handle(stream)))
+    if x.dtype != torch.bfloat16:
+        raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+    _need_cuda("x", x, weight.device)
+    if out is not None:
+        _check_out(out, x2.shape[0], weight.n, weight.device)
     y = out if out is not None else torch.empty((x2.shape[0], weight.n), dtype=torch.bfloat16, device=x.device)
     check(lib().qmm_linear(weight.handle, has_packed_u32, x2.data_ptr(), x2.shape[0], x2.stride(0),
                            y.data_ptr(), y.stride(0), _stream_handle(stream)))
@@ -556,7 +604,10 @@ class TPComm:
 
     def run_rowparallel(self, weight: QuantizedWeight, x_shard, out=None, stream=None):
         torch = _torch()
+        _need_cuda("x_shard", x_shard, weight.device)
         x2 = _as_2d(x_shard)
+        if out is not None:
+            _check_out(out, x2.shape[0], weight.n, weight.device)
         y = out if out is not None else torch.empty((x2.shape[0], weight.n), dtype=torch.bfloat16,
                                                     device=x_shard.device)
         check(lib().qmm_tp_run_rowparallel(weight.handle, self._h, x2.data_ptr(), x2.shape[0], x2.stride(0),
@@ -564,6 +615,7 @@ class TPComm:
         return y
 
     def allreduce_bf16(self, buf, stream=None):
+        _need_cuda("buf", buf)
         check(lib().qmm_tp_allreduce_bf16(self._h, buf.data_ptr(), buf.numel(), _stream_handle(stream)))
         return buf
 
