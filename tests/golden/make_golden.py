@@ -96,6 +96,38 @@ def quant_case(name, w, x, mode):
             "dequant_f32_bits": f32_bits(dq.ravel()), "y_f64": y.ravel().tolist()}
 
 
+def rule_rows(mode: str) -> np.ndarray:
+    """Hand-picked rows [r, 64] on the quantization rules' decision points: the
+    round-to-nearest-even ties of E4M3 (normal and subnormal) and E2M1,
+    saturation at 448 / 6, the scale's own ties (amax / 6 between two E4M3
+    values), and zero, tiny and huge groups.  No NaN or infinity (their
+    encodings are checked against the oracle elsewhere)."""
+    rows = []
+    pad = lambda v: np.resize(np.asarray(v, dtype=np.float64), 64)
+    if mode == "mxfp8":
+        # amax 2^8 -> X = 0: the codes are E4M3 of the values themselves.
+        ties = [(m + 0.5) / 8 * 2.0 ** e for e in (-6, -1, 0, 3, 7) for m in (8, 9, 14, 15)]
+        sub = [(q + 0.5) * 2.0 ** -9 for q in range(8)] + [2.0 ** -10, 3 * 2.0 ** -11]
+        g0 = [256.0] + ties[:31]
+        g1 = [256.0] + ties[31:] + sub + [-v for v in sub] + [1.0] * 4
+        rows.append(pad(g0 + g1[:32]))
+        rows.append(pad([500.0, 449.0, 460.0, 464.0, 470.0, 480.0, -449.0, -464.0, 447.0, 440.0] + [1.0] * 22 +
+                        [0.0] * 32))                                              # saturation; a zero group
+        rows.append(pad([1e-40, -1e-41, 5e-42] + [0.0] * 29 + [3e38, -1e38, 2.5e37] + [1.0] * 29))
+        rows.append(pad([2.0 ** (e / 4) for e in range(-40, 24)]))                # amax crossing powers of two
+    else:
+        ties = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 5.5, 0.24, 0.26, 4.9, 5.1, 6.0]
+        g = lambda scale: [6.0 * scale] + [t * scale for t in ties] + [-0.75 * scale, -5.0 * scale]
+        rows.append(pad(g(1.0) + g(2.0 ** -3) + g(2.0 ** 4) + g(2.0 ** -6)))
+        # amax / 6 on E4M3 ties: 1.0625 -> 1.0, 1.1875 -> 1.25, 2^-9 * 1.5 -> 2^-8 (subnormal scale)
+        rows.append(pad([6.0 * 1.0625, 1.0, -2.0, 3.0] + [0.5] * 12 + [6.0 * 1.1875, 1.0] + [0.25] * 14 +
+                        [6.0 * 1.5 * 2.0 ** -9, 2.0 ** -9] + [0.0] * 14 + [6.0 * 448.0 * 1.01, 1.0] + [3.0] * 14))
+        rows.append(pad([1e-4, -2e-5] + [0.0] * 14 + [0.0] * 16 + [1e4, -3e3, 7.0] + [1.0] * 13 +
+                        [1e-30, 1e-31] + [0.0] * 14))                             # zero scale, saturated scale
+        rows.append(pad([2.0 ** (e / 4) for e in range(-40, 24)]))
+    return np.asarray(rows, dtype=np.float32)
+
+
 def spec_cases() -> list[dict]:
     # src/weights.zig:493-541, restated as (tensor infos, expected) pairs.
     t = lambda name, dtype, shape: {"name": name, "dtype": dtype, "shape": shape}
@@ -141,6 +173,11 @@ def main() -> None:
         x = rng.standard_normal((3, 64)).astype(np.float32)
         x = (x.view(np.uint32) & 0xFFFF0000).view(np.float32)  # bf16-exact activations
         cases.append(quant_case(f"seeded_16x64_{mode}", w, x, mode))
+    # The rules' decision points (no RNG: appended after the seeded cases).
+    for mode in ("nvfp4", "mxfp8"):
+        w = rule_rows(mode)
+        x = np.resize(np.array([1.0, -0.5, 0.25, 2.0], dtype=np.float32), (2, 64))
+        cases.append(quant_case(f"rules_{mode}", w, x, mode))
     out = {"generator": "tests/golden/make_golden.py", "ml_dtypes": ml_dtypes.__version__,
            "numpy": np.__version__, "decode": decode_tables(), "quant_cases": cases,
            "spec_cases": spec_cases()}

@@ -36,6 +36,17 @@ def test_quantize_hard_cases(cuda_device, mode):
     assert_same(c, c_o, "codes")
 
 
+@pytest.mark.parametrize("idx", [4, 5])
+def test_quantize_independent_fixtures(cuda_device, golden, idx):
+    """The rules' decision points against the fixtures of an independent
+    quantizer (numpy + ml_dtypes casts), byte for byte."""
+    case = golden["quant_cases"][idx]
+    w = np.asarray(case["w_f32_bits"], dtype=np.uint32).view(np.float32).reshape(case["w_shape"])
+    c, s = gpu_quantize(w, case["mode"], cuda_device)
+    assert_same(c.ravel(), np.asarray(case["codes_u32"], dtype=np.uint32), "codes")
+    assert_same(s.ravel(), np.asarray(case["scales_u8"], dtype=np.uint8), "scales")
+
+
 @pytest.mark.parametrize("mode,n,k", [("mxfp8", 17408, 5120), ("nvfp4", 5120, 17408)])
 def test_quantize_config_shapes(cuda_device, mode, n, k):
     """Benchmark configs 1 and 2: W ~ N(0, 0.02^2) [N, K], seed 0."""

@@ -73,8 +73,11 @@ def test_encoders_saturate_and_tie_to_even():
     assert L.orc_decode_e4m3(L.orc_encode_e4m3(2.0 ** -10)) == 0.0  # half of the smallest subnormal
 
 
-@pytest.mark.parametrize("idx", range(4))
+@pytest.mark.parametrize("idx", range(6))
 def test_quantize_dequantize_fixtures(golden, idx):
+    """The oracle's quantizer against fixtures made by an independent one
+    (numpy + ml_dtypes casts): the reference's integer case, seeded weights
+    with planted edge values, and (idx 4, 5) the rules' decision points."""
     case = golden["quant_cases"][idx]
     w = _f32(case["w_f32_bits"]).reshape(case["w_shape"])
     codes, scales = oracle.quantize(w, case["mode"])

@@ -79,3 +79,15 @@ def test_hard_cases_cover_every_code(rules):
     b4 = c4.view(np.uint8)
     nib = set(np.unique(np.concatenate([b4 & 0xF, b4 >> 4])).tolist())
     assert nib == set(range(16))
+
+
+@pytest.mark.parametrize("idx", [4, 5])
+def test_rules_match_independent_fixtures(rules, golden, idx):
+    """The rules' decision points (ties, saturation, scale ties, zero / tiny /
+    huge groups) against the fixtures of an independent quantizer (numpy +
+    ml_dtypes casts, tests/golden/make_golden.py)."""
+    case = golden["quant_cases"][idx]
+    w = np.asarray(case["w_f32_bits"], dtype=np.uint32).view(np.float32).reshape(case["w_shape"])
+    codes, scales = host_quantize(rules, w, case["mode"])
+    assert np.array_equal(codes.ravel(), np.asarray(case["codes_u32"], dtype=np.uint32))
+    assert np.array_equal(scales.ravel(), np.asarray(case["scales_u8"], dtype=np.uint8))
