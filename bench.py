@@ -581,6 +581,32 @@ def configs_measure(args, qmm, dev) -> dict:
                       "algo_bytes": qb}
         del wq, cq, sq
     out["quantize"] = {"workload": "qmm_quantize fp32 W -> codes + scales (input larger than L2)", **qres}
+
+    # The stateless entry point (qmm_quantized_matmul: checkpoint-layout
+    # tensors, no resident state - the call-for-call counterpart of
+    # mlx_quantized_matmul) at config 2, M = 1..4; four weight copies rotate
+    # (200 MB, larger than L2).  Last in this block, and guarded, so that a
+    # failure here costs only this entry.
+    try:
+        copies2 = 4
+        draws2 = [_quantized_normal(qmm, N_OUT, K_IN, MODE, dev, seed=80 + i) for i in range(copies2)]
+        per_m = {}
+        for m in M_SET:
+            x = torch.randn((m, K_IN), device=dev).to(bf)
+            y = torch.empty((m, N_OUT), device=dev, dtype=bf)
+
+            def stateless(st):
+                for c_, s_ in draws2:
+                    qmm.quantized_matmul(x, c_, s_, mode=MODE, out=y, stream=st)
+            us = 1e3 * _graph_ms(stateless, 10) / copies2
+            gbs = algo_bytes(m) / (us * 1e-6) / 1e9
+            per_m[m] = {"us": us, "GBs": gbs, "frac": gbs / peak}
+        out["stateless"] = {"workload": "qmm_quantized_matmul (stateless, checkpoint layout) at cfg2, M = 1..4",
+                            "kernel": "gemv_kernel (csrc/gemv.cu)", "per_m": per_m, "peak": peak,
+                            "peak_kind": peak_kind}
+        del draws2
+    except Exception as exc:  # recorded, not raised: the JSON line still prints
+        out["stateless"] = {"error": repr(exc)}
     return out
 
 
