@@ -170,7 +170,8 @@ def run_reference(args, rank: int) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4xbf16->f32acc",
         "data": "synthetic (seeded N(0,1) x, N(0,0.02^2) W quantized by the oracle)",
-        "config": dict(CONFIG, copies=1, l2="CPU run, no L2 policy"),
+        "config": config_for(args.gpus),
+        "setup": {"copies": 1, "launch": "CPU, one weight copy (fp32 accumulate, OpenMP)"},
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} full steps (M=1..4, one weight copy), fp32 accumulate, "
                                    f"{threads} OpenMP threads"},
@@ -180,9 +181,17 @@ def run_reference(args, rank: int) -> None:
 
 
 METRIC = "qmm HBM GB/s, nvfp4 M=1..4 decode/MTP GEMM (K=17408, N=5120)"
-CONFIG = {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], W [5120, 17408], "
-                      "K-sharded over the GPUs, fp32 partials summed across ranks",
-          "mode": MODE, "m": list(M_SET), "n": N_OUT, "k": K_IN}
+
+
+def config_for(world: int) -> dict:
+    """The workload's `config`, printed identically by both arms: what is
+    computed, how it is split over the GPUs, and the L2 policy.  Run details
+    (weight copies, launch mode) go in the line's `setup`."""
+    return {"workload": "cfg2: nvfp4 small-batch GEMM, x bf16 [M in 1..4, 17408], W [5120, 17408], "
+                        "K-sharded over the GPUs, fp32 partials summed across ranks",
+            "mode": MODE, "m": list(M_SET), "n": N_OUT, "k": K_IN,
+            "parallelism": f"tp{world} (K-shard)" if world > 1 else "none",
+            "l2": "inputs larger than L2: weight copies rotate, so every launch streams its weights"}
 
 
 PREFILL = {"m": 32768, "n": 34816, "k": 5120, "mode": "nvfp4"}   # benchmark config 3
@@ -725,6 +734,18 @@ def bf16_peak() -> tuple[float, str]:
 
 
 def cpu_baseline_sample(budget_s: float = 10.0) -> dict:
+    """The cpu_baseline leg, run in a process of its own (this file with
+    --cpu-sample) so that its OpenMP threads do not share the host cores with
+    this process's CUDA and torch threads: the same isolation as the
+    reference arm."""
+    r = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-sample", str(budget_s)],
+                       capture_output=True, text=True, timeout=600)
+    if r.returncode != 0:
+        raise RuntimeError(f"cpu baseline subprocess failed: {r.stderr[-2000:]}")
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def _cpu_sample(budget_s: float) -> dict:
     oracle = _load("oracle", os.path.join(ROOT, "oracle", "oracle.py"))
     oracle.build()
     rng = np.random.default_rng(0)
@@ -763,7 +784,11 @@ def main() -> None:
     ap.add_argument("--prefill-warmup", type=int, default=2)
     ap.add_argument("--no-next", action="store_true", help="skip the SwiGLU / lm_head / MTP-graph measurements")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 4 / 5 measurements")
+    ap.add_argument("--cpu-sample", type=float, default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.cpu_sample is not None:       # the cpu_baseline leg's own process
+        print(json.dumps(_cpu_sample(args.cpu_sample)), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -830,8 +855,10 @@ def main() -> None:
             comm.run_rowparallel(wt, x_dev[m], out=y_dev[m], stream=cur)
 
     def step():
-        for wt in weights:
-            for m in M_SET:
+        # M-outer: consecutive launches use different weight copies, so no
+        # launch finds its weights in L2 from the launch before it.
+        for m in M_SET:
+            for wt in weights:
                 gemm(wt, m)
 
     launches_per_gemm = 1 if comm is None else 2   # GEMV (+ fp32->bf16 after the all-reduce)
@@ -1037,9 +1064,9 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4xbf16->f32acc",
             "data": "synthetic (seeded N(0,1) x; N(0,0.02^2) W drawn and quantized on the GPU by qmm_quantize)",
-            "config": dict(CONFIG, copies=copies, parallelism=f"tp{world} (K-shard)" if world > 1 else "none",
-                           launch=launch_mode,
-                           l2=f"inputs larger than L2: {copies} weight copies x {shard_bytes / 1e6:.1f} MB rotate"),
+            "config": config_for(world),
+            "setup": {"copies": copies, "launch": launch_mode,
+                      "l2": f"{copies} weight copies x {shard_bytes / 1e6:.1f} MB rotate (L2 126 MB)"},
             "tflops": step_flops(copies) * args.steps / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,

@@ -137,7 +137,37 @@ int current_device(int* dev) {
     return device_info(*dev, &info);
 }
 
+// The stateless entry points take raw pointers and launch on the current
+// device: each one must be device (or managed) memory that device can use.
+// A host pointer, or another GPU's buffer, handed to a kernel or a TMA map
+// would fault the device instead of failing the call.
+int check_on_device(const void* p, int dev, const char* what) {
+    if (!p) return QMM_OK;
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();   // the query's error must not linger for the next call
+        return set_error(QMM_ERR_BAD_ARGUMENT, "%s: not a CUDA pointer (%s)", what, cudaGetErrorString(e));
+    }
+    if (attr.type == cudaMemoryTypeManaged) return QMM_OK;
+    if (attr.type != cudaMemoryTypeDevice)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "%s is host memory; the call needs device memory", what);
+    if (attr.device != dev)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "%s lives on device %d, the current device is %d", what,
+                         attr.device, dev);
+    return QMM_OK;
+}
+
+int check_stateless_ptrs(int dev, const void* x, const void* y, const void* w, const void* scales) {
+    if (int rc = check_on_device(x, dev, "x")) return rc;
+    if (int rc = check_on_device(y, dev, "y")) return rc;
+    if (int rc = check_on_device(w, dev, "w")) return rc;
+    return check_on_device(scales, dev, "scales");
+}
+
 }  // namespace
+
+int check_device_buffer(const void* p, int dev, const char* what) { return check_on_device(p, dev, what); }
 }  // namespace qmm
 
 using namespace qmm;
@@ -199,6 +229,7 @@ extern "C" int qmm_quantized_matmul(void* y_dev, int64_t ldy, const void* x_dev,
     if (!w_dev || !scales_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "w or scales is NULL");
     int dev;
     if (int rc = current_device(&dev)) return rc;
+    if (int rc = check_stateless_ptrs(dev, x_dev, y_dev, w_dev, scales_dev)) return rc;
     QmmArgs a;
     a.fmt = format_of(spec);
     a.codes = reinterpret_cast<const uint8_t*>(w_dev);
@@ -239,6 +270,7 @@ extern "C" int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy, const void
     if (!w_dev || !scales_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "w or scales is NULL");
     int dev;
     if (int rc = current_device(&dev)) return rc;
+    if (int rc = check_stateless_ptrs(dev, x_dev, y_dev, w_dev, scales_dev)) return rc;
     QmmArgs a;
     a.fmt = format_of(spec);
     a.codes = reinterpret_cast<const uint8_t*>(w_dev);
@@ -451,12 +483,16 @@ extern "C" int qmm_weight_info(const qmm_weight* w, int64_t* n, int64_t* k, qmm_
 
 namespace {
 
-int weight_args(const qmm_weight* w, QmmArgs* a) {
+// The weight's geometry for a launch on the current device, which must be
+// the weight's; x and y (either may be NULL) must be memory of that device.
+int weight_args(const qmm_weight* w, QmmArgs* a, const void* x, const void* y) {
     if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
     int dev;
     if (int rc = current_device(&dev)) return rc;
     if (dev != w->device)
         return set_error(QMM_ERR_BAD_ARGUMENT, "weight lives on device %d, current device is %d", w->device, dev);
+    if (int rc = check_on_device(x, dev, "x")) return rc;
+    if (int rc = check_on_device(y, dev, "y")) return rc;
     a->fmt = format_of(w->spec);
     a->codes = w->codes;
     a->ldc = w->ldc;
@@ -478,7 +514,7 @@ extern "C" int qmm_run(const qmm_weight* w, const void* x_dev, int64_t m, int64_
     if (int rc = check_xy(x_dev, m, w->k, ldx, y_dev, w->n, ldy)) return rc;
     if (m == 0 || w->n == 0) return QMM_OK;
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, x_dev, y_dev)) return rc;
     a.x = static_cast<const uint16_t*>(x_dev);
     a.ldx = ldx;
     a.y = static_cast<uint16_t*>(y_dev);
@@ -505,7 +541,9 @@ extern "C" int qmm_lm_head_argmax(const qmm_weight* w, const void* x_dev, int64_
     }
     if (w->n > INT32_MAX) return set_error(QMM_ERR_BAD_SHAPE, "n=%lld exceeds 32-bit indices", (long long)w->n);
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, x_dev, logits_dev)) return rc;
+    if (int rc = check_on_device(ids_dev, w->device, "ids")) return rc;
+    if (int rc = check_on_device(logprobs_dev, w->device, "logprobs")) return rc;
     a.x = static_cast<const uint16_t*>(x_dev);
     a.ldx = ldx;
     a.y = static_cast<uint16_t*>(logits_dev);
@@ -547,7 +585,7 @@ extern "C" int qmm_swiglu_run(const qmm_weight* w, const void* x_dev, int64_t m,
     if (int rc = check_xy(x_dev, m, w->k, ldx, h_dev, w->swiglu_n, ldh)) return rc;
     if (m == 0) return QMM_OK;
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, x_dev, h_dev)) return rc;
     a.x = static_cast<const uint16_t*>(x_dev);
     a.ldx = ldx;
     a.y = static_cast<uint16_t*>(h_dev);
@@ -590,7 +628,7 @@ extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dt
     if (out_dtype != QMM_DTYPE_BF16 && out_dtype != QMM_DTYPE_F32)
         return set_error(QMM_ERR_UNSUPPORTED_DTYPE, "dequantize output dtype %d (BF16 or F32)", out_dtype);
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, nullptr, out_dev)) return rc;
     if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight has no single dequantized form");
     if (w->n == 0) return QMM_OK;
     if (!out_dev) return set_error(QMM_ERR_BAD_ARGUMENT, "out is NULL");
@@ -640,7 +678,7 @@ int run_rowparallel_fused(const qmm_weight* w, const TpExchange* ex, const void*
     if ((reinterpret_cast<uintptr_t>(x_dev) & 15) || ((ldx * 2) & 15))
         return set_error(QMM_ERR_BAD_ARGUMENT, "row-parallel decode needs 16-byte aligned x rows");
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, x_dev, y_dev)) return rc;
     a.x = static_cast<const uint16_t*>(x_dev);
     a.ldx = ldx;
     a.y = static_cast<uint16_t*>(y_dev);
@@ -656,7 +694,7 @@ int run_partial_f32(const qmm_weight* w, const void* x_dev, int64_t m, int64_t l
                     cudaStream_t stream) {
     if (int rc = check_xy(x_dev, m, w ? w->k : 0, ldx, yf, w ? w->n : 0, ldy)) return rc;
     QmmArgs a;
-    if (int rc = weight_args(w, &a)) return rc;
+    if (int rc = weight_args(w, &a, x_dev, yf)) return rc;
     a.x = static_cast<const uint16_t*>(x_dev);
     a.ldx = ldx;
     a.y = nullptr;

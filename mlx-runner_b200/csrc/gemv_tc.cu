@@ -440,11 +440,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             }
             named_sync(1, kConsumers * 32);
             if (t == 0) {
+                // One system-scope release fence, then relaxed flag stores:
+                // the fence and each later strong store form a release
+                // pattern (the barrier above ordered every thread's pushes
+                // before the fence), so the P flags cost one fence, not P.
                 asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll
                 for (int r = 0; r < kMaxTpRanks; ++r)
                     if (r < P)
-                        asm volatile("st.release.sys.global.u32 [%0], %1;"
+                        asm volatile("st.relaxed.sys.global.u32 [%0], %1;"
                                      ::"l"(p.tp_flags[r] + me * p.tp_max_rb + rb), "r"(epoch) : "memory");
                 p.tp_gen[rb] = epoch;
                 const int n_list = s_tp_list[0];

@@ -40,6 +40,9 @@ struct DeviceInfo {
     size_t smem_optin = 0;
 };
 int device_info(int device, DeviceInfo* out);
+// QMM_OK when p is NULL, or device / managed memory that device `dev` can
+// use; BadArgument (naming `what`) for host memory or another GPU's buffer.
+int check_device_buffer(const void* p, int dev, const char* what);
 
 // ---- kernels -----------------------------------------------------------------
 // Peer-memory exchange of a row-parallel (K-sharded) decode: every rank's

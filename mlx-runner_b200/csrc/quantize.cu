@@ -114,6 +114,9 @@ int launch_quantize(int fmt, const void* w, bool w_bf16, int64_t ldw, int64_t n,
     QMM_CUDA_TRY(cudaGetDevice(&dev));
     DeviceInfo info;
     if (int rc = device_info(dev, &info)) return rc;
+    if (int rc = check_device_buffer(w, dev, "w")) return rc;
+    if (int rc = check_device_buffer(codes, dev, "codes")) return rc;
+    if (int rc = check_device_buffer(scales, dev, "scales")) return rc;
     const int64_t chunks = n * (k / 4);
     const int64_t want = (chunks + 255) / 256;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(want, static_cast<int64_t>(info.sms) * 8));

@@ -256,11 +256,26 @@ def _check_out(out, rows: int, cols: int, device: Optional[int] = None) -> None:
                           f"got {tuple(out.shape)} {out.dtype}")
 
 
+def _need_current(name: str, t) -> None:
+    """The stateless entry points launch on the current CUDA device: a tensor
+    on another device would hand that device's pointers to this one."""
+    cur = _torch().cuda.current_device()
+    if t.device.index != cur:
+        raise QmmError(7, f"{name} is on cuda:{t.device.index} but the current device is cuda:{cur}; "
+                          f"call under `with torch.cuda.device({t.device.index})`")
+
+
 def _need_packed(w, scales) -> None:
+    torch = _torch()
     _need_cuda("w", w)
     _need_cuda("scales", scales, w.device.index)
+    _need_current("w", w)
     if w.dim() != 2 or scales.dim() != 2 or not w.is_contiguous() or not scales.is_contiguous():
         raise QmmError(7, "w and scales must be contiguous 2-D tensors (the checkpoint layout)")
+    if w.dtype not in (torch.int32, getattr(torch, "uint32", torch.int32)):
+        raise QmmError(5, f"w must hold the packed U32 words (int32 or uint32), got {w.dtype}")
+    if scales.dtype != torch.uint8:
+        raise QmmError(5, f"scales must be uint8, got {scales.dtype}")
 
 
 def quantized_matmul(x, w, scales, biases=None, transpose: bool = True, group_size: Optional[int] = None,
@@ -327,6 +342,7 @@ def quantize(w, mode: str = "mxfp8", group_size: Optional[int] = None, bits: Opt
     if w.dim() != 2:
         raise QmmError(1, f"quantize takes a 2-D weight, got shape {tuple(w.shape)}")
     _need_cuda("w", w)
+    _need_current("w", w)
     if w.stride(1) != 1:
         w = w.contiguous()
     spec = spec_from_args(group_size, bits, mode)

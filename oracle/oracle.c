@@ -238,6 +238,67 @@ int orc_qmm_f64(int mode, const uint16_t* x, int64_t m, int64_t ldx,
     return bad ? -1 : 0;
 }
 
+/* y and sum_k |x| |W| in one pass, for checks at full benchmark sizes (no
+ * [N, K] intermediate).  Four partial sums per dot product keep the fp64
+ * adds from forming one long dependency chain; in fp64 the order changes the
+ * result by ~1e-16 relative, far below every bar the tests apply.  A NaN
+ * weight contributes NaN to y and 0 to the absolute sum (as abs_qmm_f64). */
+int orc_qmm_f64_abs(int mode, const uint16_t* x, int64_t m, int64_t ldx,
+                    const uint8_t* codes, const uint8_t* scales, int64_t n, int64_t k,
+                    double* y, double* yabs) {
+    int group, bits;
+    if (spec_of(mode, &group, &bits) || m < 0 || n < 0 || k <= 0 || k % group || ldx < k) return -1;
+    const int64_t row_bytes = k * bits / 8, ng = k / group;
+    double* xd = (double*)malloc(sizeof(double) * (size_t)(2 * m * k + 1));
+    if (!xd) return -1;
+    double* xa = xd + m * k;
+    for (int64_t i = 0; i < m; ++i)
+        for (int64_t kk = 0; kk < k; ++kk) {
+            xd[i * k + kk] = orc_bf16_to_f32(x[i * ldx + kk]);
+            xa[i * k + kk] = fabs(xd[i * k + kk]);
+        }
+    int bad = 0;
+    #pragma omp parallel
+    {
+        double* w = (double*)malloc(sizeof(double) * (size_t)(2 * k));
+        if (!w) {
+            #pragma omp atomic write
+            bad = 1;
+        } else {
+            double* wa = w + k;
+            #pragma omp for schedule(dynamic, 16)
+            for (int64_t r = 0; r < n; ++r) {
+                const uint8_t* cr = codes + r * row_bytes;
+                for (int64_t kk = 0; kk < k; ++kk) {
+                    w[kk] = (double)elem_of(mode, code_at(cr, bits, kk)) *
+                            (double)scale_of(mode, scales[r * ng + kk / group]);
+                    wa[kk] = isnan(w[kk]) ? 0.0 : fabs(w[kk]);
+                }
+                for (int64_t i = 0; i < m; ++i) {
+                    const double* xr = xd + i * k;
+                    const double* ar = xa + i * k;
+                    double s[4] = {0, 0, 0, 0}, t[4] = {0, 0, 0, 0};
+                    int64_t kk = 0;
+                    for (; kk + 4 <= k; kk += 4)
+                        for (int j = 0; j < 4; ++j) {
+                            s[j] += xr[kk + j] * w[kk + j];
+                            t[j] += ar[kk + j] * wa[kk + j];
+                        }
+                    for (; kk < k; ++kk) {
+                        s[0] += xr[kk] * w[kk];
+                        t[0] += ar[kk] * wa[kk];
+                    }
+                    y[i * n + r] = (s[0] + s[1]) + (s[2] + s[3]);
+                    yabs[i * n + r] = (t[0] + t[1]) + (t[2] + t[3]);
+                }
+            }
+            free(w);
+        }
+    }
+    free(xd);
+    return bad ? -1 : 0;
+}
+
 int orc_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

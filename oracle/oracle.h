@@ -77,6 +77,12 @@ int orc_qmm_f64(int mode, const uint16_t* x, int64_t m, int64_t ldx,
                 const uint8_t* codes, const uint8_t* scales, int64_t n, int64_t k,
                 double* y);
 
+/* orc_qmm_f64 and, in yabs [M, N], sum_k |x[m, k]| * |W[n, k]| (NaN weights
+ * count 0): the scale of the accumulation error, in one pass over W. */
+int orc_qmm_f64_abs(int mode, const uint16_t* x, int64_t m, int64_t ldx,
+                    const uint8_t* codes, const uint8_t* scales, int64_t n, int64_t k,
+                    double* y, double* yabs);
+
 /* The timed CPU baseline: dequantize on the fly, fp32 accumulate, bf16
  * output (RNE) [M, N].  Uses `threads` OpenMP threads (<=0: all). */
 int orc_qmm_f32(int mode, const uint16_t* x, int64_t m, int64_t ldx,

@@ -62,7 +62,8 @@ def lib() -> ctypes.CDLL:
         L.orc_dequantize.argtypes = [ctypes.c_int, vp, vp, i64, i64, vp]
         L.orc_qmm_f64.argtypes = [ctypes.c_int, vp, i64, i64, vp, vp, i64, i64, vp]
         L.orc_qmm_f32.argtypes = [ctypes.c_int, vp, i64, i64, vp, vp, i64, i64, vp, ctypes.c_int]
-        for fn in (L.orc_quantize, L.orc_dequantize, L.orc_qmm_f64, L.orc_qmm_f32):
+        L.orc_qmm_f64_abs.argtypes = [ctypes.c_int, vp, i64, i64, vp, vp, i64, i64, vp, vp]
+        for fn in (L.orc_quantize, L.orc_dequantize, L.orc_qmm_f64, L.orc_qmm_f32, L.orc_qmm_f64_abs):
             fn.restype = ctypes.c_int
         L.orc_max_threads.restype = ctypes.c_int
         _lib = L
@@ -112,6 +113,38 @@ def qmm_f64(x_bf16: np.ndarray, codes: np.ndarray, scales: np.ndarray, mode: str
     if lib().orc_qmm_f64(MODES[mode], _p(x_bf16), m, k, _p(codes), _p(scales), n, k, _p(y)):
         raise ValueError("orc_qmm_f64 rejected its arguments")
     return y
+
+
+def qmm_f64_abs(x_bf16: np.ndarray, codes: np.ndarray, scales: np.ndarray, mode: str):
+    """(qmm_f64, abs_qmm_f64) in one pass over W without an [N, K]
+    intermediate: the checker at full benchmark sizes."""
+    group, bits = SPEC[mode]
+    x_bf16 = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    codes = np.ascontiguousarray(codes, dtype=np.uint32)
+    scales = np.ascontiguousarray(scales, dtype=np.uint8)
+    m, k = x_bf16.shape
+    n = codes.shape[0]
+    assert codes.shape[1] * 32 // bits == k
+    y = np.empty((m, n), dtype=np.float64)
+    ya = np.empty((m, n), dtype=np.float64)
+    if m < 16:
+        # Few x rows: one pass over W in C, each row dequantized once.
+        if lib().orc_qmm_f64_abs(MODES[mode], _p(x_bf16), m, k, _p(codes), _p(scales), n, k, _p(y), _p(ya)):
+            raise ValueError("orc_qmm_f64_abs rejected its arguments")
+        return y, ya
+    # Many x rows: exact fp32 dequantisation of W in row blocks, then fp64
+    # matrix products (every product of a bf16 and a dequantised value is
+    # exact in fp64; only the fp64 summation order differs from qmm_f64).
+    xd = bf16_bits_to_f32(x_bf16).astype(np.float64)
+    xa = np.abs(xd)
+    block = max(256, (1 << 25) // max(1, k))
+    for r0 in range(0, n, block):
+        w = dequantize(codes[r0:r0 + block], scales[r0:r0 + block], mode).astype(np.float64)
+        y[:, r0:r0 + block] = xd @ w.T
+        np.abs(w, out=w)
+        w[np.isnan(w)] = 0.0
+        ya[:, r0:r0 + block] = xa @ w.T
+    return y, ya
 
 
 def qmm_f32(x_bf16: np.ndarray, codes: np.ndarray, scales: np.ndarray, mode: str,

@@ -67,3 +67,16 @@ def test_reference_arm_prints_the_contract_line():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["config"]["workload"].startswith("cfg2")
+
+
+def test_both_arms_print_one_config(bench):
+    """The GPU arm and the reference arm print the same `config` for the same
+    world size (run details live in `setup`), so the driver's comparison of
+    the two lines sees one workload."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "0", "--gpus", "2"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["config"] == bench.config_for(2)
+    assert bench.config_for(1)["parallelism"] == "none"
+    assert "copies" not in line["config"] and "launch" not in line["config"]

@@ -85,10 +85,45 @@ def test_output_buffers_must_hold_the_result():
             qmm._check_out(bad, 3, 64, 0)
 
 
-def test_packed_tensors_must_be_contiguous_and_together():
+@pytest.fixture
+def current_cuda0(monkeypatch):
+    """torch.cuda.current_device() == 0 without a GPU."""
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+
+
+def test_packed_tensors_must_be_contiguous_and_together(current_cuda0):
     w = FakeCuda((8, 4), dtype=torch.int32)
     qmm._need_packed(w, FakeCuda((8, 2), dtype=torch.uint8))
     with pytest.raises(qmm.QmmError):
         qmm._need_packed(w, FakeCuda((8, 2), dtype=torch.uint8, device=1))
     with pytest.raises(qmm.QmmError):
         qmm._need_packed(FakeCuda((8, 4), dtype=torch.int32, contiguous=False), FakeCuda((8, 2), dtype=torch.uint8))
+
+
+def test_packed_tensors_must_have_the_packed_dtypes(current_cuda0):
+    """Codes are the U32 words (int32 / uint32) and scales bytes: a float or
+    int64 tensor of the right shape would be read as the wrong bytes."""
+    s = FakeCuda((8, 2), dtype=torch.uint8)
+    qmm._need_packed(FakeCuda((8, 4), dtype=torch.int32), s)
+    for bad in (torch.int64, torch.float32, torch.uint8, torch.bfloat16):
+        with pytest.raises(qmm.QmmError) as ei:
+            qmm._need_packed(FakeCuda((8, 4), dtype=bad), s)
+        assert name_of(ei) == "UnsupportedDtype"
+    for bad in (torch.int32, torch.float32, torch.int8):
+        with pytest.raises(qmm.QmmError) as ei:
+            qmm._need_packed(FakeCuda((8, 4), dtype=torch.int32), FakeCuda((8, 2), dtype=bad))
+        assert name_of(ei) == "UnsupportedDtype"
+
+
+def test_stateless_calls_need_the_current_device(monkeypatch):
+    """The stateless entry points launch on the current device: tensors that
+    all live on cuda:1 while cuda:0 is current are refused, not launched on
+    device 0 with device 1's pointers."""
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    w = FakeCuda((8, 4), dtype=torch.int32, device=1)
+    s = FakeCuda((8, 2), dtype=torch.uint8, device=1)
+    with pytest.raises(qmm.QmmError) as ei:
+        qmm._need_packed(w, s)
+    assert name_of(ei) == "BadArgument" and "current device is cuda:0" in str(ei.value)
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 1)
+    qmm._need_packed(w, s)                                       # current device 1: accepted

@@ -43,10 +43,18 @@ def check_sampling(w, x, codes, scales, mode):
     ids, lp, ids2, lp2 = ids.cpu().numpy(), lp.cpu().numpy(), ids2.cpu().numpy(), lp2.cpu().numpy()
     np.testing.assert_array_equal(ids, ids2)
     np.testing.assert_array_equal(lp.view(np.uint32), lp2.view(np.uint32))
+    check_logits_and_ids(ids, lp, y, x, codes, scales, mode)
+    return ids, lp
+
+
+def check_logits_and_ids(ids, lp, y, x, codes, scales, mode):
+    """The logits y meet the qmm bar against the fp64 oracle; ids / lp are the
+    greedy sample of those logits (lowest index among equal values; lp within
+    1 bf16 ulp of the logsumexp) and each id's exact logit is within the bar
+    of the exact maximum."""
     yb = bits(y)
     xb = bits(x)
-    ref = oracle.qmm_f64(xb, codes, scales, mode)
-    absref = oracle.abs_qmm_f64(xb, codes, scales, mode)
+    ref, absref = oracle.qmm_f64_abs(xb, codes, scales, mode)
     assert oracle.parity_violations(oracle.bf16_bits_to_f32(yb), ref, absref) == 0
     want_ids, want_lp = oracle.greedy_sample(yb)
     np.testing.assert_array_equal(ids, want_ids)
@@ -57,7 +65,6 @@ def check_sampling(w, x, codes, scales, mode):
         top = np.max(ref[r])
         tol = oracle.bf16_ulp(top) + 2.0 ** -20 * absref[r, ids[r]]
         assert ref[r, ids[r]] >= top - 2 * tol
-    return ids, lp
 
 
 @pytest.mark.parametrize("mode", ["mxfp8", "nvfp4"])
@@ -79,6 +86,29 @@ def test_argmax_vocab_slice(cuda_device, m):
     w = qmm.QuantizedWeight(codes, scales, mode)
     x = make_x(m, k, seed=m).to(cuda_device)
     check_sampling(w, x, codes, scales, mode)
+
+
+def random_packed(n, k, seed):
+    """nvfp4 [n, k] as random packed words (every E2M1 code) and UE4M3 scales
+    in [2^-7, 2^-3): built directly, without an [n, k] fp32 draw."""
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0, 2 ** 32, (n, k // 8), dtype=np.uint32)
+    scales = rng.integers(0x18, 0x38, (n, k // 16), dtype=np.uint8)
+    return codes, scales
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_argmax_full_vocab(cuda_device, m):
+    """The whole [248320, 5120] nvfp4 lm_head (src/model.zig:1300-1310
+    logitsOf, all 248320 rows) with greedy sampling, M = 1 (decode) and M = 3
+    (MTP verify): every logit against the fp64 oracle, the id and log-
+    probability against the oracle's sampling of the kernel's logits."""
+    n, k, mode = 248320, 5120, "nvfp4"
+    codes, scales = random_packed(n, k, seed=12)
+    w = qmm.QuantizedWeight(codes, scales, mode)
+    x = make_x(m, k, seed=20 + m).to(cuda_device)
+    check_sampling(w, x, codes, scales, mode)
+    w.close()
 
 
 def test_argmax_ties_take_lowest_index(cuda_device):

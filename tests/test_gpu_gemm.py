@@ -19,8 +19,7 @@ pytestmark = pytest.mark.gpu
 def sampled_parity(y_gpu, x, codes, scales, mode, rows, frob=2e-3):
     xs = x[rows].contiguous()
     xb = bits(xs)
-    ref = oracle.qmm_f64(xb, codes, scales, mode)
-    absref = oracle.abs_qmm_f64(xb, codes, scales, mode)
+    ref, absref = oracle.qmm_f64_abs(xb, codes, scales, mode)
     y = oracle.bf16_bits_to_f32(bits(y_gpu[rows]))
     assert oracle.parity_violations(y, ref, absref) == 0
     rf = oracle.rel_frobenius(y, ref)
@@ -109,14 +108,58 @@ def test_config_shapes_sampled(cuda_device, name, mode, m, n, k):
     _torch_check(y, x, w)
 
 
+def sample_rows(m, seed, count=512):
+    """`count` distinct seeded token rows: the first and last rows, both sides
+    of the 128-, 256- and 512-token tile edges near the start, the middle and
+    the end, and seeded random rows for the rest."""
+    edges = {0, 1, 127, 128, 255, 256, 511, 512, m // 2 - 1, m // 2, m - 513, m - 512, m - 257, m - 256,
+             m - 129, m - 128, m - 2, m - 1}
+    rows = {r for r in edges if 0 <= r < m}
+    rng = np.random.default_rng(seed)
+    while len(rows) < min(count, m):
+        rows.update(rng.integers(0, m, count - len(rows)).tolist())
+    return sorted(rows)[:count] if len(rows) > count else sorted(rows)
+
+
 def test_cfg3_full_32k_prefill(cuda_device):
-    """Benchmark config 3 at full size: x [32768, 5120], W [34816, 5120] nvfp4."""
+    """Benchmark config 3 at full size: x [32768, 5120], W [34816, 5120] nvfp4;
+    512 seeded token rows (every output column) against the fp64 oracle, and
+    the whole tensor against torch over the exact bf16 dequantisation."""
     m, n, k = 32768, 34816, 5120
     codes, scales = make_weight(n, k, "nvfp4", seed=0)
     x = make_x(m, k, seed=0).to(cuda_device)
     w = qmm.QuantizedWeight(codes, scales, "nvfp4")
     y = w(x)
     qmm.device_status()
-    rows = sorted({0, 255, 256, 16383, 32767} | set(np.random.default_rng(1).integers(0, m, 27).tolist()))
+    rows = sample_rows(m, seed=1)
+    assert len(rows) == 512
     sampled_parity(y, x, codes, scales, "nvfp4", rows)
     _torch_check(y, x, w)
+
+
+# Benchmark config 4: the prefill GEMMs of one GDN layer (mxfp8, T = 32768),
+# the reference's call sites src/model.zig:1066-1075 (in_proj_qkv|z and b|a,
+# concatenated along N), :1230 (out_proj) and :905-915 (gate/up, down).
+CFG4 = [("in_proj_qkvz", 16384, 5120), ("in_proj_ba", 96, 5120), ("out_proj", 5120, 6144),
+        ("gate_up", 34816, 5120), ("down", 5120, 17408)]
+
+
+@pytest.mark.parametrize("name,n,k", CFG4, ids=[c[0] for c in CFG4])
+def test_cfg4_full_32k_prefill(cuda_device, name, n, k):
+    """Each config 4 projection at the benchmarked T = 32768: 512 seeded token
+    rows against the fp64 oracle (per element and relative Frobenius) and the
+    full tensor against torch over the exact bf16 dequantisation."""
+    import torch
+    m, mode = 32768, "mxfp8"
+    codes, scales = make_weight(n, k, mode, seed=n + k)
+    x = make_x(m, k, seed=k).to(cuda_device)
+    w = qmm.QuantizedWeight(codes, scales, mode)
+    y = w(x)
+    qmm.device_status()
+    rows = sample_rows(m, seed=n)
+    assert len(rows) == 512
+    sampled_parity(y, x, codes, scales, mode, rows)
+    _torch_check(y, x, w)
+    w.close()
+    del x, y
+    torch.cuda.empty_cache()

@@ -6,8 +6,11 @@ model's shapes, nvfp4.
 Capture needs every entry point on the path to be allocation- and
 sync-free; a replay must give the eager results bit for bit (the
 kernels are deterministic, including the stream-K reductions and the
-argmax / logsumexp merges).  The per-op numerics are covered by the
-parity tests; here the weights are random packed bytes made on the GPU.
+argmax / logsumexp merges).  The step's outputs are also checked against
+the CPU oracle, each linear on the input it actually read: fc (K = 10240),
+q / k / v, o_proj, the SwiGLU pair, down, and the M = 1 draft / M = 3
+verify sampling through the whole 248320-row lm_head.  The weights are
+random packed bytes made on the GPU (every E2M1 code, finite scales).
 """
 import numpy as np
 import pytest
@@ -28,15 +31,24 @@ def rand_weight(n, k, dev, seed):
     return codes, scales
 
 
-def build_step(dev):
+def build_step(dev, raw=None):
     """Weights of the MTP head linears and lm_head (shapes from the model:
     fc 10240 -> 5120, q_proj 5120 -> 12288, k/v 5120 -> 1024, o_proj
     6144 -> 5120, gate/up 5120 -> 17408, down 17408 -> 5120, lm_head
-    5120 -> 248320)."""
+    5120 -> 248320).  `raw`, when given, receives each weight's packed
+    (codes, scales) device tensors ("gate" / "up" for the SwiGLU pair)."""
     shapes = {"fc": (H, 2 * H), "q": (12288, H), "k": (1024, H), "v": (1024, H), "o": (H, 6144),
               "down": (H, FFN), "lm_head": (VOCAB, H)}
-    w = {name: qmm.QuantizedWeight(*rand_weight(n, k, dev, i), "nvfp4") for i, (name, (n, k)) in enumerate(shapes.items())}
-    w["mlp"] = qmm.SwiGLUWeight(*rand_weight(FFN, H, dev, 20), *rand_weight(FFN, H, dev, 21), "nvfp4")
+    w = {}
+    for i, (name, (n, k)) in enumerate(shapes.items()):
+        cs = rand_weight(n, k, dev, i)
+        w[name] = qmm.QuantizedWeight(*cs, "nvfp4")
+        if raw is not None:
+            raw[name] = cs
+    gate, up = rand_weight(FFN, H, dev, 20), rand_weight(FFN, H, dev, 21)
+    w["mlp"] = qmm.SwiGLUWeight(*gate, *up, "nvfp4")
+    if raw is not None:
+        raw["gate"], raw["up"] = gate, up
     return w
 
 
@@ -111,3 +123,59 @@ def test_mtp_step_graph_replays_eager_results(cuda_device):
     ids = bufs["verify_ids"].cpu().numpy()
     assert np.all((ids >= 0) & (ids < VOCAB))
     del graph
+
+
+def _host(cs):
+    import torch
+    c, sc = cs
+    return c.cpu().numpy().view(np.uint32), sc.cpu().numpy()
+
+
+def _bits(t):
+    import torch
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def test_mtp_step_outputs_match_oracle(cuda_device):
+    """One eager MTP step (src/mtp.zig:137-191: fc over [embed | hidden], the
+    head's attention projections, MLP; src/engine.zig:548 / :656 verify
+    sampling), each output against the fp64 oracle on the input the kernel
+    read, and the sampled ids / log-probabilities against the oracle's greedy
+    sampling of the lm_head's logits."""
+    import torch
+    import oracle
+    from test_gpu_argmax import check_logits_and_ids
+    raw = {}
+    w = build_step(cuda_device, raw)
+    bufs = make_bufs(cuda_device)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        run_step(w, bufs, s)
+    s.synchronize()
+    qmm.device_status()
+    # Each linear: (weight, input buffer, output buffer).
+    for name, xin, yout in (("fc", "cat", "fused"), ("q", "fused", "q"), ("k", "fused", "k"), ("v", "fused", "v"),
+                            ("o", "attn", "o"), ("down", "ff", "mp")):
+        codes, scales = _host(raw[name])
+        ref, absref = oracle.qmm_f64_abs(_bits(bufs[xin]), codes, scales, "nvfp4")
+        got = oracle.bf16_bits_to_f32(_bits(bufs[yout]))
+        assert oracle.parity_violations(got, ref, absref) == 0, name
+        assert oracle.rel_frobenius(got, ref) <= 2e-3, name
+    # SwiGLU: h = silu(x . Wg^T) * (x . Wu^T) on the o_proj output.
+    xb = _bits(bufs["o"])
+    g_ref, g_abs = oracle.qmm_f64_abs(xb, *_host(raw["gate"]), "nvfp4")
+    u_ref, u_abs = oracle.qmm_f64_abs(xb, *_host(raw["up"]), "nvfp4")
+    assert oracle.swiglu_violations(_bits(bufs["ff"]), g_ref, u_ref, g_abs, u_abs) == 0
+    # Sampling: the step's ids / log-probabilities are the greedy sample of
+    # the lm_head's own logits, which meet the qmm bar.
+    lm = w["lm_head"]
+    codes, scales = _host(raw["lm_head"])
+    for xin, id_key, lp_key in (("mp", "draft_id", "draft_lp"), ("verify_x", "verify_ids", "verify_lp")):
+        ids, lp, logits = lm.argmax(bufs[xin], logits=True)
+        torch.cuda.synchronize()
+        step_ids, step_lp = bufs[id_key].cpu().numpy(), bufs[lp_key].cpu().numpy()
+        np.testing.assert_array_equal(step_ids, ids.cpu().numpy())
+        np.testing.assert_array_equal(step_lp.view(np.uint32), lp.cpu().numpy().view(np.uint32))
+        check_logits_and_ids(step_ids, step_lp, logits, bufs[xin], codes, scales, "nvfp4")
+    for x in w.values():
+        x.close()

@@ -1,7 +1,8 @@
-"""Tensor parallelism on 2 GPUs (one process per GPU): K-sharded row-parallel
-GEMM with the cross-rank sum, and N-sharded column-parallel shards
-(no collective), both checked against the CPU oracle; skipped with fewer
-than 2 GPUs.  On one GPU: the exchange's bounded wait running out.
+"""Tensor parallelism on 2, 4 and 8 GPUs (one process per GPU): K-sharded
+row-parallel GEMM with the cross-rank sum, and N-sharded column-parallel
+shards (no collective), both checked against the CPU oracle; each world
+size is skipped where fewer GPUs are visible.  On one GPU: the exchange's
+bounded wait running out.
 """
 import os
 import sys
@@ -52,15 +53,18 @@ def _rank(rank, world, uid, mode, n, k, m, q):
         q.put((rank, repr(exc), None))
 
 
-@pytest.mark.parametrize("mode,n,k,m", [("nvfp4", 1024, 4096, 3), ("mxfp8", 768, 2048, 1)])
-def test_tp_two_gpus(mode, n, k, m):
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode,n,k,m", [("nvfp4", 1024, 4096, 3), ("mxfp8", 768, 2048, 1),
+                                        ("nvfp4", 5120, 17408, 4)])
+def test_tp_gpus(world, mode, n, k, m):
+    """K = 17408 / N = 5120 is benchmark config 2 (K slices of 8704 / 4352 /
+    2176 codes); the smaller cases put few row blocks on each rank."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import multiprocessing as mp
     import oracle
     import qmm
-    world = 2
     uid = qmm.TPComm.unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -69,7 +73,7 @@ def test_tp_two_gpus(mode, n, k, m):
         p.start()
     out = {}
     for _ in range(world):
-        rank, a, b = q.get(timeout=300)
+        rank, a, b = q.get(timeout=600)
         out[rank] = (a, b)
     for p in procs:
         p.join(timeout=120)
@@ -78,8 +82,7 @@ def test_tp_two_gpus(mode, n, k, m):
         assert not isinstance(a, str), f"rank {rank}: {a}"
 
     codes, scales, x = _case(mode, n, k, m, seed=9)
-    ref = oracle.qmm_f64(x, codes, scales, mode)
-    absref = oracle.abs_qmm_f64(x, codes, scales, mode)
+    ref, absref = oracle.qmm_f64_abs(x, codes, scales, mode)
     for rank in range(world):
         y = oracle.bf16_bits_to_f32(out[rank][0])
         assert oracle.parity_violations(y, ref, absref) == 0
