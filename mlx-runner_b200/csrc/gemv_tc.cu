@@ -395,6 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         const int cw = warp - kFirstConsumer, rg = cw & 7, kh = cw >> 3;
         const int g = lane >> 2, c = lane & 3;
         const int r0 = 16 * rg + g, r1 = r0 + 8;
+        // B-fragment lane 4 n + c carries x only when its column n holds an x
+        // row < M (kXlGroups2: n = 2 c + t, so only lanes with g / 2 == c and
+        // t < M); the other lanes' slots are zero for the whole launch, so
+        // they skip the shared-memory load (M <= 2 reads 1/8 - 1/4 of the
+        // fragment bytes).
+        const bool x_live = (XL == kXlGroups2 && FMT == kNVFP4) ? ((g >> 1) == c && (g & 1) < p.m) : (g < p.m);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
         // Static schedule: CTA j owns units [first_unit(j), first_unit(j + 1));
@@ -774,7 +780,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
                         const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
                         // da / db: two chains over the step pair's two mmas.
-                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        uint4 bx = make_uint4(0u, 0u, 0u, 0u);
+                        if (x_live) bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         mma16816(da, a0, bx.x, bx.y);
                         mma16816(db, a1, bx.z, bx.w);
                     }
@@ -850,7 +857,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                             ha[b] = hmul2u(ha[b], sa);
                             hb[b] = hmul2u(hb[b], sbv);
                         }
-                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        uint4 bx = make_uint4(0u, 0u, 0u, 0u);
+                        if (x_live) bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
                         const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
                         const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
@@ -884,7 +892,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         a[1] = e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFF));
                         a[2] = e4m3x2_to_f16x2((uint16_t)(wa >> 16));
                         a[3] = e4m3x2_to_f16x2((uint16_t)(wb >> 16));
-                        const uint2 b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
+                        uint2 b = make_uint2(0u, 0u);
+                        if (x_live) b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
                         mma16816(d, a, b.x, b.y);
                     }
                     const float sc0 = ue8m0_to_f32((sw0 >> (8 * gi)) & 0xFF);

@@ -256,7 +256,10 @@ def swiglu_violations(h_bits: np.ndarray, g_ref: np.ndarray, u_ref: np.ndarray, 
     """Elements of h = silu(g) * u (bf16 bits) outside the exact composition's
     band: the gate / up sums may each miss by the GEMM bar (1 bf16 ulp +
     acc_rel * sum|x||w|), carried through silu(g) * u by its derivatives,
-    plus the four bf16 roundings of the chain (2^-8 relative each)."""
+    plus the four bf16 roundings of the chain (2^-8 relative each), plus the
+    fp32 range of the sigmoid: a sigmoid evaluated in fp32 - MLX's of a bf16
+    array, or the kernels' - is 0 once e^-g overflows (g < -87.3), where the
+    exact value is below 2^-126, so h may miss by |g| |u| 2^-126 there."""
     h = bf16_bits_to_f32(h_bits).astype(np.float64)
     g, u = np.asarray(g_ref, np.float64), np.asarray(u_ref, np.float64)
     with np.errstate(over="ignore", invalid="ignore"):
@@ -267,7 +270,7 @@ def swiglu_violations(h_bits: np.ndarray, g_ref: np.ndarray, u_ref: np.ndarray, 
     tg = bf16_ulp(g) + acc_rel * absg
     tu = bf16_ulp(u) + acc_rel * absu
     tol = (np.abs(dsilu) * tg * (np.abs(u) + tu) + (np.abs(silu) + np.abs(dsilu) * tg) * tu
-           + 4.0 * 2.0 ** -8 * np.abs(ref) + 2.0 ** -133)
+           + 4.0 * 2.0 ** -8 * np.abs(ref) + (np.abs(g) + tg) * (np.abs(u) + tu) * 2.0 ** -126 + 2.0 ** -133)
     bad = ~(np.abs(h - ref) <= tol)
     both_nan = np.isnan(h) & np.isnan(ref)
     return int(np.count_nonzero(bad & ~both_nan))
