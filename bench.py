@@ -724,6 +724,36 @@ def cfg5_tp_measure(qmm, dev, world: int, rank: int, comm, barrier, max_over_ran
             "peak": peak, "peak_kind": peak_kind, "kv_replicated": kv_rep}
 
 
+def _tensor_peaks() -> dict:
+    """Dense tcgen05 rates of this GPU per MMA kind (qmm_tensor_peak), best of
+    three launches each after one warm-up: the denominators of the prefill
+    fractions (bf16 for the exact path, the block-scaled kinds for the
+    x-quantised one)."""
+    import torch
+    torch.cuda.set_device(0)
+    qmm = _load("qmm", os.path.join(PKG, "qmm.py"))
+    out = {}
+    for kind in ("bf16", "mxf8f6f4", "mxf4nvf4"):
+        qmm.tensor_peak(kind, 1 << 12)
+        out[kind] = max(qmm.tensor_peak(kind, 1 << 16) for _ in range(3))
+    return out
+
+
+def tensor_peaks_measure() -> dict:
+    """_tensor_peaks in a process of its own (this file with --tensor-peaks),
+    so that nothing it does can touch this process's CUDA context."""
+    r = subprocess.run([sys.executable, os.path.abspath(__file__), "--tensor-peaks"], capture_output=True, text=True,
+                       timeout=600)
+    if r.returncode != 0:
+        return {"error": r.stderr[-1500:]}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    d["unit"] = "TFLOP/s"
+    d["how"] = ("qmm_tensor_peak: one CTA per SM issuing back-to-back tcgen05.mma 128x256 (kind::f16 K16, "
+                "kind::mxf8f6f4.block_scale K32, kind::mxf4nvf4.block_scale.block16 K64) on resident tiles; "
+                "best of 3 launches of 65536 MMA pairs per SM")
+    return d
+
+
 def bf16_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -785,9 +815,13 @@ def main() -> None:
     ap.add_argument("--no-next", action="store_true", help="skip the SwiGLU / lm_head / MTP-graph measurements")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 / 4 / 5 measurements")
     ap.add_argument("--cpu-sample", type=float, default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--tensor-peaks", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.cpu_sample is not None:       # the cpu_baseline leg's own process
         print(json.dumps(_cpu_sample(args.cpu_sample)), flush=True)
+        return
+    if args.tensor_peaks:                 # the tensor-peak measurement's own process
+        print(json.dumps(_tensor_peaks()), flush=True)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1058,6 +1092,12 @@ def main() -> None:
             return float(t.item())
         configs = {"cfg5": cfg5_tp_measure(qmm, dev, world, rank, comm, barrier, max_over_ranks, sum_over_ranks)}
 
+    tensor_peaks = tensor_peaks_measure() if world == 1 and not args.no_configs else None
+    if prefill is not None and tensor_peaks and "bf16" in tensor_peaks:
+        tp = prefill["roofline"]["achieved"]
+        prefill["roofline"]["frac_of_tcgen05_bf16_peak"] = tp / tensor_peaks["bf16"]
+        prefill["roofline"]["frac_of_mxf4nvf4_peak"] = tp / tensor_peaks["mxf4nvf4"]
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -1080,6 +1120,7 @@ def main() -> None:
             "prefill": prefill,
             "next_rows": next_rows,
             "configs": configs,
+            "tensor_peaks": tensor_peaks,
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()

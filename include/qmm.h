@@ -130,7 +130,17 @@ int qmm_spec_from_args(qmm_optional_int group_size, qmm_optional_int bits, const
  *   biases     must be NULL (mxfp8/nvfp4 are bias-less, src/model.zig:230-232)
  *   transpose  must be true (the only form the reference uses, model.zig:253)
  *   y_dev      bf16 [M, N], row stride ldy (elements)
- * Reads the scales in their checkpoint layout; needs no workspace. */
+ * Every pointer must be memory of the current device (checked before any
+ * launch: host memory or another GPU's buffer is QMM_ERR_BAD_ARGUMENT).
+ * Reads the codes and scales in their checkpoint layout.  For M <= 8 with
+ * 16-byte aligned x / code / scale rows it runs qmm_run's tensor-core decode
+ * kernel, reading both tensors by TMA; its stream-K scratch (1.2 MB of
+ * partial sums, 256 KB of counters) is a workspace the library makes on the
+ * first call on each (device, stream) and keeps until the process exits.
+ * That first call allocates and so cannot be captured in a CUDA graph (it
+ * fails with QMM_ERR_BAD_ARGUMENT inside a capture): make one call on a
+ * stream before capturing it.  Calls on different streams never share a
+ * workspace.  Other shapes run a workspace-free split-K kernel. */
 int qmm_quantized_matmul(void* y_dev, int64_t ldy,
                          const void* x_dev, int64_t m, int64_t k, int64_t ldx,
                          const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
@@ -154,7 +164,9 @@ int qmm_quantized_matmul(void* y_dev, int64_t ldy,
  *     (cudaGetSymbolAddress): make it before any stream capture begins;
  *   - calls that overlap in time on one device share the array and race:
  *     order them on one stream;
- *   - the array keeps the last call's contents after it returns. */
+ *   - the array keeps the last call's contents after it returns;
+ *   - the address is cached per device for the life of the process: after a
+ *     cudaDeviceReset the entry point is unusable until the process restarts. */
 int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy,
                                  const void* x_dev, int64_t m, int64_t k, int64_t ldx,
                                  const uint32_t* w_dev, int64_t w_rows, int64_t w_cols,
@@ -362,6 +374,30 @@ int qmm_fault_arm(uint64_t k);
 int qmm_fault_fired(void);
 
 int qmm_abi_version(void);
+
+/* x-quantised prefill on the block-scaled tensor cores - NOT the parity
+ * path, no counterpart in the reference's own code (MLX's block-scaled
+ * kernels are the closest analogue).  y[M, N] = q(x) . dequant(W)^T, where
+ * q(x) quantises each 16-value group of x to nvfp4 by qmm_quantize's rules
+ * (E2M1 codes, UE4M3 scale) and the product runs as tcgen05.mma
+ * kind::mxf4nvf4.block_scale on the packed codes of both operands, fp32
+ * accumulation, bf16 out.  Quantising x costs about 10% relative error, far
+ * outside qmm_run's parity bar: callers opt in by calling this entry point.
+ * nvfp4 weights only, K a multiple of 32.  The first call on a weight builds
+ * its scale-factor tiles (allocates; not inside a graph capture); every call
+ * takes its x scratch (about M*K*9/16 bytes) from the stream-ordered
+ * allocator. */
+int qmm_run_blockscaled(qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* y_dev, int64_t ldy,
+                        void* stream);
+
+/* Measurement hook, no counterpart in the reference: the dense tcgen05 MMA
+ * rate of the current device for one MMA kind (0 = kind::f16 bf16, 1 =
+ * kind::mxf8f6f4 E4M3 with UE8M0 scales per 32, 2 = kind::mxf4nvf4 E2M1 with
+ * UE4M3 scales per 16), from one timed launch of `iters` back-to-back
+ * 128 x 256 MMA pairs per SM on `stream`; *tflops receives the rate.  These
+ * are the roofline denominators of the prefill GEMMs (bench.py).
+ * Synchronizes `stream`. */
+int qmm_tensor_peak(int kind, int64_t iters, void* stream, double* tflops);
 
 #ifdef __cplusplus
 }

@@ -241,7 +241,15 @@ extern "C" int qmm_quantized_matmul(void* y_dev, int64_t ldy, const void* x_dev,
     a.y = static_cast<uint16_t*>(y_dev);
     a.ldy = ldy;
     a.m = m; a.n = n; a.k = k;
-    return dispatch(a, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (m <= gemv_max_m()) {
+        // Decode / MTP-verify rows: the TMA decode kernel on the tensors as
+        // they are; outside its envelope, the cluster split-K GEMV.
+        bool handled = false;
+        if (int rc = launch_gemv_tc_ckpt(a, s, &handled)) return rc;
+        if (handled) return QMM_OK;
+    }
+    return dispatch(a, s);
 }
 
 extern "C" int qmm_quantized_matmul_noalloc(void* y_dev, int64_t ldy, const void* x_dev, int64_t m, int64_t k,
@@ -463,6 +471,7 @@ extern "C" int qmm_weight_destroy(qmm_weight* w) {
     cudaGetDevice(&prev);
     if (w->device >= 0) cudaSetDevice(w->device);
     gemv_tc_release(w);
+    cudaFree(w->bs_sf);
     cudaError_t e1 = cudaFree(w->codes);
     cudaError_t e2 = cudaFree(w->scales);
     if (prev >= 0) cudaSetDevice(prev);
@@ -621,6 +630,36 @@ extern "C" int qmm_linear(const qmm_weight* w, bool has_packed_u32, const void* 
     if (!w && has_packed_u32) return set_error(QMM_ERR_MISSING_WEIGHT, "packed weight has no scales");
     if (!w) return set_error(QMM_ERR_MISSING_WEIGHT, "weight is missing");
     return qmm_run(w, x_dev, m, ldx, y_dev, ldy, true, stream);
+}
+
+extern "C" int qmm_run_blockscaled(qmm_weight* w, const void* x_dev, int64_t m, int64_t ldx, void* y_dev,
+                                   int64_t ldy, void* stream) {
+    QMM_FAULT_POINT("qmm_run_blockscaled");
+    if (!w) return set_error(QMM_ERR_BAD_ARGUMENT, "weight is NULL");
+    if (w->swiglu_n > 0) return set_error(QMM_ERR_BAD_ARGUMENT, "a gate/up weight runs through qmm_swiglu_run");
+    if (w->spec.mode != QMM_MODE_NVFP4)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "the block-scaled GEMM takes nvfp4 weights");
+    if (int rc = check_xy(x_dev, m, w->k, ldx, y_dev, w->n, ldy)) return rc;
+    if (m == 0 || w->n == 0) return QMM_OK;
+    if (w->k % 32) return set_error(QMM_ERR_BAD_SHAPE, "block-scaled GEMM: k=%lld is not a multiple of 32",
+                                    (long long)w->k);
+    QmmArgs a;
+    if (int rc = weight_args(w, &a, x_dev, y_dev)) return rc;
+    a.x = static_cast<const uint16_t*>(x_dev);
+    a.ldx = ldx;
+    a.y = static_cast<uint16_t*>(y_dev);
+    a.ldy = ldy;
+    a.m = m;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!w->bs_sf) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMM_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+            return set_error(QMM_ERR_BAD_ARGUMENT, "the first qmm_run_blockscaled call on a weight allocates its "
+                                                   "scale atoms and cannot be captured");
+        if (int rc = make_gemm_bs_weight_sf(a, &w->bs_sf, s)) return rc;
+    }
+    return launch_gemm_blockscaled(a, w->bs_sf, s);
 }
 
 extern "C" int qmm_dequantize(const qmm_weight* w, void* out_dev, int32_t out_dtype, void* stream) {

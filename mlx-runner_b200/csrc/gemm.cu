@@ -644,8 +644,11 @@ extern "C" int qmm_device_status(void* stream) {
         QMM_CUDA_TRY(cudaMemcpyToSymbolAsync(qmm::g_device_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s));
         QMM_CUDA_TRY(cudaStreamSynchronize(s));
     }
-    unsigned int v2 = 0;
+    unsigned int v2 = 0, v3 = 0;
     QMM_CUDA_TRY(qmm::gemv_tc_take_error(&v2, s));
+    QMM_CUDA_TRY(qmm::gemm_bs_take_error(&v3, s));
+    v |= v3;
+    if (v2) qmm::gemv_tc_mark_workspaces_dirty();   // stream-K counters may be left set
     if (v | v2) return qmm::set_error(QMM_ERR_TIMEOUT, "a device-side wait timed out (flags 0x%x)", v | v2);
     return QMM_OK;
 }

@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvParams p) {
 template <int FMT, int M, bool VEC16>
 int launch_m(const GemvParams& p, int rows_per_warp_hint, int nsplit, cudaStream_t stream) {
     (void)rows_per_warp_hint;
-    constexpr int R = (M <= 2) ? 8 : (M <= 4 ? 4 : 2);
+    constexpr int R = (M <= 1) ? 8 : (M <= 4 ? 4 : 2);   // M = 2 with 8 rows needs > 128 registers
     constexpr int RB = kWarps * R;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((p.n + RB - 1) / RB), (unsigned)nsplit, 1);
@@ -289,7 +289,7 @@ int launch_fmt(const GemvParams& p, int m, int nsplit, cudaStream_t stream) {
     return set_error(QMM_ERR_BAD_SHAPE, "gemv: m=%d outside 1..8", m);
 }
 
-inline int rows_per_warp(int m) { return (m <= 2) ? 8 : (m <= 4 ? 4 : 2); }
+inline int rows_per_warp(int m) { return (m <= 1) ? 8 : (m <= 4 ? 4 : 2); }
 
 // Number of K-splits (cluster size): the smallest power of two giving at
 // least ~4 CTAs per SM, while each lane keeps >= 2 chunks per split.

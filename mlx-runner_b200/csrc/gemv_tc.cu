@@ -38,9 +38,12 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "formats.cuh"
 #include "internal.h"
@@ -97,6 +100,7 @@ struct TcParams {
     unsigned int* am_done;
     // Row-parallel exchange (tp_n > 1): final row-block sums go to every
     // rank's receive slot over NVLink and are added there in rank order.
+    int l2_prefetch;   // 1: prefetch the CTA's weight range beyond the ring into L2 up front
     int tp_n, tp_rank, tp_max_rb;
     int64_t tp_cap;
     float* tp_recv[kMaxTpRanks];
@@ -153,6 +157,16 @@ __device__ __forceinline__ void bulk_1d(void* dst, const void* src, uint32_t byt
                  ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// L2 prefetch of a 2D TMA box / a contiguous range (no shared memory, no
+// barrier): the bytes are in L2 when the matching load is issued later.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x0, int y0) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(y0) : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -203,12 +217,29 @@ constexpr int kXlTokens = 0, kXlGroups2 = 1;
 // others' code and registers.
 constexpr int kEpiPlain = 0, kEpiSwiglu = 1, kEpiArgmax = 2, kEpiTp = 3;
 
-template <int FMT, int XL, int EPI>
+// Where a unit's scales come from:
+//   kScaleTiled  the per-unit [128 rows][SB] tiles made at weight creation
+//                (one bulk copy per unit);
+//   kScaleCkpt   the checkpoint's U8 [N, K/group] tensor itself (stateless
+//                calls): a 2D TMA box of 128 rows; for mxfp8 the box is 16
+//                bytes wide (the TMA minimum) and the unit's 8 bytes start at
+//                (kc & 1) * 8 inside it.
+constexpr int kScaleTiled = 0, kScaleCkpt = 1;
+
+template <int FMT, int SRC> struct ScaleLayout {
+    static constexpr int SB = Cfg<FMT>::SB;
+    static constexpr int kStride = (SRC == kScaleCkpt && FMT == kMXFP8) ? 16 : SB;   // smem row stride
+    static constexpr int kBytes = kRows * kStride;                                    // per stage
+};
+
+template <int FMT, int XL, int EPI, int SRC>
 __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_constant__ CUtensorMap cmap,
                                                                    const __grid_constant__ CUtensorMap xmap,
+                                                                   const __grid_constant__ CUtensorMap smap,
                                                                    TcParams p) {
-    constexpr int KC = Cfg<FMT>::KC, SB = Cfg<FMT>::SB;
-    constexpr int kScaleBytes = kRows * SB;
+    constexpr int KC = Cfg<FMT>::KC;
+    constexpr int SB = ScaleLayout<FMT, SRC>::kStride;     // bytes per row of a staged scale tile
+    constexpr int kScaleBytes = ScaleLayout<FMT, SRC>::kBytes;
     constexpr int kXRawBytes = kXRows * KC * 2;
     constexpr int kXfBytes = kXRows * KC * 2;
     extern __shared__ uint8_t smem_raw[];
@@ -265,8 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes);
                 tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], w_kc * 256, w_rb * kRows);
                 tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], w_kc * 256 + 128, w_rb * kRows);
-                bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)(u0 + i) * kScaleBytes, kScaleBytes,
-                        &full[s]);
+                if constexpr (SRC == kScaleCkpt)
+                    tma_2d(s_scales + s * kScaleBytes, &smap, &full[s], (w_kc * Cfg<FMT>::SB) & ~15, w_rb * kRows);
+                else
+                    bulk_1d(s_scales + s * kScaleBytes, p.scales_tiled + (int64_t)(u0 + i) * kScaleBytes,
+                            kScaleBytes, &full[s]);
                 if (++w_kc == p.kchunks) { w_kc = 0; ++w_rb; }
             };
             auto issue_x = [&](int i) {
@@ -280,8 +314,24 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             // The first ring of weight tiles streams before the wait on the
             // previous grid (programmatic dependent launch): only x (and the
             // outputs, written after x is consumed) depend on earlier kernels.
+            // The rest of this CTA's weight range is prefetched into L2 as
+            // well, so HBM streams this launch's weights while the previous
+            // launch finishes (its tail and stream-K fix-up); every weight
+            // byte is still read from HBM once.
             const int pre = min(kStages, nunits);
             for (int i = 0; i < pre; ++i) issue_w(i);
+            if (p.l2_prefetch) {
+                int f_rb = w_rb, f_kc = w_kc;
+                for (int i = pre; i < nunits; ++i) {
+                    tma_prefetch_2d(&cmap, f_kc * 256, f_rb * kRows);
+                    tma_prefetch_2d(&cmap, f_kc * 256 + 128, f_rb * kRows);
+                    if constexpr (SRC == kScaleCkpt)
+                        tma_prefetch_2d(&smap, (f_kc * Cfg<FMT>::SB) & ~15, f_rb * kRows);
+                    else
+                        bulk_prefetch_l2(p.scales_tiled + (int64_t)(u0 + i) * kScaleBytes, kScaleBytes);
+                    if (++f_kc == p.kchunks) { f_kc = 0; ++f_rb; }
+                }
+            }
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int i = 0; i < pre; ++i) issue_x(i);
             int last = pre - 1;
@@ -873,8 +923,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             } else {
                 // mxfp8: step j covers k [16j, 16j + 16) (one half group);
                 // thread c owns bytes 16j + 4c .. + 3 of each row.
-                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB + 4 * kh);
-                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB + 4 * kh);
+                const int soff = (SRC == kScaleCkpt) ? (kc & 1) * 8 : 0;   // the unit's 8 bytes in a 16-byte box row
+                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB + soff + 4 * kh);
+                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB + soff + 4 * kh);
 #pragma unroll
                 for (int gi = 0; gi < 4; ++gi) {
                     const int grp = 4 * kh + gi;         // this warp's four 32-code groups
@@ -949,37 +1000,65 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
     return fn;
 }
 
-template <int FMT>
+template <int FMT, int SRC = kScaleTiled>
 constexpr int smem_bytes() {
-    return 1024 + kStages * (kCodeBytes + kRows * Cfg<FMT>::SB + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
+    return 1024 + kStages * (kCodeBytes + ScaleLayout<FMT, SRC>::kBytes + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
            kRows * 8 * 4 + 512;
 }
 
-using GemvTcKernel = void (*)(CUtensorMap, CUtensorMap, TcParams);
+using GemvTcKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcParams);
 
-// Kernel for a format and M, with its dynamic shared memory configured once
-// per device.  nvfp4 takes the group-slot x layout for M <= 2 (the scale
-// leaves the per-code path); QMM_XL=0 keeps the token layout (for A/B runs).
-int pick_kernel(int fmt, int64_t m, int epi, int dev, GemvTcKernel* fn, int* smem) {
+// Up-front L2 prefetch of each CTA's weight range beyond its ring: off unless
+// QMM_L2_PREFETCH=1 (measured slower on config 2 and the lm_head).
+int l2_prefetch_enabled() {
+    static const int on = [] {
+        const char* e = getenv("QMM_L2_PREFETCH");
+        return (e && e[0] == '1') ? 1 : 0;
+    }();
+    return on;
+}
+
+// Kernel for a format, M, epilogue and scale source, with its dynamic shared
+// memory configured once per device.  nvfp4 takes the group-slot x layout
+// for M <= 2 (the scale leaves the per-code path); QMM_XL=0 keeps the token
+// layout (for A/B runs).  Checkpoint-layout scales (stateless calls) come
+// with the plain epilogue only.
+int pick_kernel(int fmt, int64_t m, int epi, int src, int dev, GemvTcKernel* fn, int* smem) {
     static const bool tokens_only = [] {
         const char* e = getenv("QMM_XL");
         return e && e[0] == '0';
     }();
-    // One table row per (format / layout), one column per epilogue.
-    static const GemvTcKernel table[3][4] = {
-        {qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiArgmax>, qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiTp>},
-        {qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiArgmax>, qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiTp>},
-        {qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiPlain>, qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiSwiglu>,
-         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiArgmax>, qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiTp>},
+    // One table row per (format / layout), one column per epilogue, then the
+    // checkpoint-scale plain kernels.
+    static const GemvTcKernel table[3][5] = {
+        {qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiPlain, kScaleTiled>,
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiSwiglu, kScaleTiled>,
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiArgmax, kScaleTiled>,
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiTp, kScaleTiled>,
+         qmm_gemv_tc_kernel<kMXFP8, kXlTokens, kEpiPlain, kScaleCkpt>},
+        {qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiPlain, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiSwiglu, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiArgmax, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiTp, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlGroups2, kEpiPlain, kScaleCkpt>},
+        {qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiPlain, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiSwiglu, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiArgmax, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiTp, kScaleTiled>,
+         qmm_gemv_tc_kernel<kNVFP4, kXlTokens, kEpiPlain, kScaleCkpt>},
     };
+    if (src == kScaleCkpt && epi != kEpiPlain)
+        return set_error(QMM_ERR_BAD_ARGUMENT, "checkpoint-layout scales run the plain epilogue only");
     const int row = fmt == kMXFP8 ? 0 : (!tokens_only && m <= 2) ? 1 : 2;
-    *smem = fmt == kMXFP8 ? smem_bytes<kMXFP8>() : smem_bytes<kNVFP4>();
-    *fn = table[row][epi];
-    const int slot = row * 4 + epi;
+    const int col = src == kScaleCkpt ? 4 : epi;
+    if (fmt == kMXFP8)
+        *smem = src == kScaleCkpt ? smem_bytes<kMXFP8, kScaleCkpt>() : smem_bytes<kMXFP8>();
+    else
+        *smem = src == kScaleCkpt ? smem_bytes<kNVFP4, kScaleCkpt>() : smem_bytes<kNVFP4>();
+    *fn = table[row][col];
+    const int slot = row * 5 + col;
     static std::mutex mu;
-    static bool configured[12][64] = {};
+    static bool configured[15][64] = {};
     if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!configured[slot][dev]) {
@@ -1128,6 +1207,7 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     p.am_part = st->am_part;
     p.am_done = reinterpret_cast<unsigned int*>(st->am_keys + 8);
     if (a.argmax_ids && (p.tp_n > 0 || a.yf || a.swiglu_n > 0)) return QMM_OK;
+    p.l2_prefetch = l2_prefetch_enabled();
     p.partial = st->partial;
     p.counters = st->counters;
     p.ldy = a.ldy;
@@ -1157,9 +1237,9 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     GemvTcKernel fn = nullptr;
     int smem = 0;
     const int epi = a.argmax_ids ? kEpiArgmax : a.swiglu_n > 0 ? kEpiSwiglu : p.tp_n > 1 ? kEpiTp : kEpiPlain;
-    if (int rc = pick_kernel(fmt, a.m, epi, w->device, &fn, &smem)) return rc;
+    if (int rc = pick_kernel(fmt, a.m, epi, kScaleTiled, w->device, &fn, &smem)) return rc;
     cfg.dynamicSmemBytes = smem;
-    QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, st->cmap, xmap, p));
+    QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, st->cmap, xmap, st->cmap, p));   // smap unused (tiled scales)
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;
     return QMM_OK;
@@ -1268,6 +1348,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.swiglu_n = 0;
     p.am_ids = nullptr;
     p.am_lp = nullptr;
+    p.l2_prefetch = l2_prefetch_enabled();
     p.partial = reinterpret_cast<float*>(base + partial_off);
     p.counters = counters;
     p.ldy = a.ldy;
@@ -1279,8 +1360,169 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.units = (int)units;
     GemvTcKernel fn = nullptr;
     int smem = 0;
-    if (int rc = pick_kernel(fmt, a.m, kEpiPlain, dev, &fn, &smem)) return rc;
-    fn<<<(unsigned)grid, kThreads, smem, stream>>>(cmap, xmap, p);
+    if (int rc = pick_kernel(fmt, a.m, kEpiPlain, kScaleTiled, dev, &fn, &smem)) return rc;
+    fn<<<(unsigned)grid, kThreads, smem, stream>>>(cmap, xmap, cmap, p);   // smap unused (tiled scales)
+    QMM_CUDA_TRY(cudaGetLastError());
+    *handled = true;
+    return QMM_OK;
+}
+
+}  // namespace qmm
+
+// ---- stateless calls on checkpoint-layout tensors ------------------------------
+//
+// qmm_quantized_matmul (the mlx_quantized_matmul counterpart) runs the same
+// decode kernel on the caller's U32 codes and U8 scales as they lie in the
+// checkpoint: codes by the 2D TMA boxes of the resident path, scales by 2D
+// TMA boxes of the [N, K/group] tensor (no re-tiled copy).  The stream-K
+// partial sums and row-block counters live in a workspace owned by the
+// library, one per (device, stream), made on the first call on that stream
+// and kept until the process exits: calls on one stream are ordered, calls on
+// different streams use different workspaces.  The counters return to zero at
+// the end of every call; after a kernel that gave up a bounded wait
+// (qmm_device_status reports Timeout) every workspace is zeroed again before
+// its next use.
+
+namespace qmm {
+namespace {
+
+constexpr int64_t kWsMaxRowBlocks = int64_t(1) << 16;   // N up to 8,388,608 rows
+
+struct StreamWorkspace {
+    float* partial = nullptr;           // [grid][2][128][8]
+    unsigned int* counters = nullptr;   // [kWsMaxRowBlocks]
+    int grid = 0;
+    uint64_t zeroed_gen = 0;            // dirty generation the counters were zeroed at
+};
+
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, StreamWorkspace> g_ws;
+std::atomic<uint64_t> g_ws_dirty_gen{1};
+
+int stream_workspace(int dev, cudaStream_t stream, int sms, StreamWorkspace** out) {
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    auto it = g_ws.find({dev, stream});
+    if (it == g_ws.end()) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QMM_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+            return set_error(QMM_ERR_BAD_ARGUMENT,
+                             "the first qmm_quantized_matmul call on a stream allocates its workspace and cannot be "
+                             "captured: make one call on this stream before capturing it");
+        StreamWorkspace ws;
+        ws.grid = sms;
+        cudaError_t e = cudaMalloc(&ws.partial, (size_t)sms * 2 * kRows * 8 * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&ws.counters, (size_t)kWsMaxRowBlocks * sizeof(unsigned int));
+        if (e != cudaSuccess) {
+            cudaFree(ws.partial);
+            return cuda_error(e, "cudaMalloc(stateless workspace)");
+        }
+        it = g_ws.emplace(std::make_pair(dev, stream), ws).first;
+    }
+    StreamWorkspace& ws = it->second;
+    const uint64_t gen = g_ws_dirty_gen.load();
+    if (ws.zeroed_gen != gen) {
+        QMM_CUDA_TRY(cudaMemsetAsync(ws.counters, 0, (size_t)kWsMaxRowBlocks * sizeof(unsigned int), stream));
+        ws.zeroed_gen = gen;
+    }
+    *out = &ws;
+    return QMM_OK;
+}
+
+}  // namespace
+
+void gemv_tc_mark_workspaces_dirty() { g_ws_dirty_gen.fetch_add(1); }
+
+int launch_gemv_tc_ckpt(const QmmArgs& a, cudaStream_t stream, bool* handled) {
+    *handled = false;
+    if (a.yf || a.m < 1 || a.m > kXRows) return QMM_OK;
+    if (a.n <= 0 || a.n > INT32_MAX || a.k > INT32_MAX) return QMM_OK;
+    const int fmt = a.fmt;
+    const int KC = fmt == kMXFP8 ? Cfg<kMXFP8>::KC : Cfg<kNVFP4>::KC;
+    const int group = fmt == kMXFP8 ? 32 : 16;
+    const int64_t ngroups = a.k / group;
+    const int64_t row_blocks = (a.n + kRows - 1) / kRows, kchunks = (a.k + KC - 1) / KC;
+    // TMA envelope: 16-byte aligned x / code / scale rows.
+    const auto xa = reinterpret_cast<uintptr_t>(a.x), ca = reinterpret_cast<uintptr_t>(a.codes),
+               sa = reinterpret_cast<uintptr_t>(a.scales);
+    if ((xa & 15) || ((a.ldx * 2) & 15) || (ca & 15) || (a.ldc & 15) || (sa & 15) || (a.lds & 15)) return QMM_OK;
+    if (row_blocks > kWsMaxRowBlocks || kchunks * row_blocks > INT32_MAX) return QMM_OK;
+    auto enc = encoder();
+    if (!enc) return QMM_OK;
+    int dev = 0;
+    QMM_CUDA_TRY(cudaGetDevice(&dev));
+    DeviceInfo info;
+    if (int rc = device_info(dev, &info)) return rc;
+    if (info.smem_optin < (size_t)smem_bytes<kNVFP4, kScaleCkpt>()) return QMM_OK;
+    CUtensorMap cmap, xmap, smap;
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)(a.k * (fmt == kMXFP8 ? 8 : 4) / 8), (cuuint64_t)a.n};
+        const cuuint64_t gstride[1] = {(cuuint64_t)a.ldc};
+        const cuuint32_t box[2] = {128, (cuuint32_t)kRows};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.codes), gdim, gstride, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return QMM_OK;
+    }
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
+        const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
+        const cuuint32_t box[2] = {256u, (cuuint32_t)a.m};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return QMM_OK;
+    }
+    {
+        // One unit's scales: 128 rows of SB bytes (nvfp4: 32), or of a 16-byte
+        // box holding the unit's 8 bytes (mxfp8).
+        const cuuint64_t gdim[2] = {(cuuint64_t)ngroups, (cuuint64_t)a.n};
+        const cuuint64_t gstride[1] = {(cuuint64_t)a.lds};
+        const cuuint32_t box[2] = {fmt == kMXFP8 ? 16u : (cuuint32_t)Cfg<kNVFP4>::SB, (cuuint32_t)kRows};
+        const cuuint32_t es[2] = {1, 1};
+        if (enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.scales), gdim, gstride, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return QMM_OK;
+    }
+    StreamWorkspace* ws = nullptr;
+    if (int rc = stream_workspace(dev, stream, info.sms, &ws)) return rc;
+    const int64_t units = kchunks * row_blocks;
+    const int grid = (int)std::min<int64_t>(units, ws->grid);
+    TcParams p;
+    p.scales_tiled = nullptr;
+    p.y = a.y;
+    p.yf = nullptr;
+    p.tp_n = 0;
+    p.swiglu_n = 0;
+    p.am_ids = nullptr;
+    p.am_lp = nullptr;
+    p.l2_prefetch = l2_prefetch_enabled();
+    p.partial = ws->partial;
+    p.counters = ws->counters;
+    p.ldy = a.ldy;
+    p.m = (int)a.m;
+    p.n = (int)a.n;
+    p.k = (int)a.k;
+    p.kchunks = (int)kchunks;
+    p.row_blocks = (int)row_blocks;
+    p.units = (int)units;
+    GemvTcKernel fn = nullptr;
+    int smem = 0;
+    if (int rc = pick_kernel(fmt, a.m, kEpiPlain, kScaleCkpt, dev, &fn, &smem)) return rc;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, cmap, xmap, smap, p));
     QMM_CUDA_TRY(cudaGetLastError());
     *handled = true;
     return QMM_OK;

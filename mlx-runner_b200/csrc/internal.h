@@ -133,8 +133,22 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
 // The same kernel on checkpoint-layout weights with its scratch in a static
 // device array (no allocation); errors if the weight needs more than it holds.
 int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled);
+// The same kernel on checkpoint-layout weights and scales (TMA boxes of the
+// caller's tensors) with its stream-K scratch in a per-(device, stream)
+// workspace made on the first call on that stream (not during capture).
+int launch_gemv_tc_ckpt(const QmmArgs& a, cudaStream_t stream, bool* handled);
+// After a kernel gave up a bounded wait: zero every workspace's counters
+// before its next use.
+void gemv_tc_mark_workspaces_dirty();
 // Read and clear the kernel's device-side timeout word (synchronizes s).
 cudaError_t gemv_tc_take_error(unsigned int* v, cudaStream_t s);
+
+// x-quantised prefill GEMM on the block-scaled tensor cores (gemm_bs.cu):
+// y = quantize_nvfp4(x) . dequant(W)^T.  Not the parity path.  w_sf holds
+// the weight's scale atoms (make_gemm_bs_weight_sf, once per weight).
+int launch_gemm_blockscaled(const QmmArgs& a, const uint8_t* w_sf, cudaStream_t stream);
+int make_gemm_bs_weight_sf(const QmmArgs& a, uint8_t** out, cudaStream_t stream);
+cudaError_t gemm_bs_take_error(unsigned int* v, cudaStream_t s);
 
 }  // namespace qmm
 
@@ -149,4 +163,5 @@ struct qmm_weight {
     uint8_t* scales = nullptr;  // device, row stride lds
     int64_t lds = 0;
     int64_t swiglu_n = 0;       // > 0: gate / up pair interleaved in 64-row blocks (qmm_swiglu_weight_create)
+    uint8_t* bs_sf = nullptr;   // scale atoms of the block-scaled GEMM, made on its first call
 };

@@ -51,6 +51,7 @@ EXPORTS = (
     "qmm_tp_comm_create", "qmm_tp_comm_create_detached", "qmm_tp_comm_destroy", "qmm_tp_allreduce_bf16",
     "qmm_tp_run_rowparallel",
     "qmm_last_error", "qmm_error_pending", "qmm_device_status", "qmm_fault_arm", "qmm_fault_fired",
+    "qmm_tensor_peak", "qmm_run_blockscaled",
 )
 
 
@@ -138,6 +139,8 @@ def lib() -> ctypes.CDLL:
     L.qmm_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.qmm_fault_arm.argtypes = [ctypes.c_uint64]
     L.qmm_device_status.argtypes = [vp]
+    L.qmm_tensor_peak.argtypes = [i32, i64, vp, ctypes.POINTER(ctypes.c_double)]
+    L.qmm_run_blockscaled.argtypes = [vp, vp, i64, i64, vp, i64, vp]
     for name in EXPORTS:
         fn = getattr(L, name)
         if name != "qmm_mode_str":
@@ -163,6 +166,18 @@ def take_error() -> tuple[int, str]:
 def device_status(stream=None) -> None:
     """Raise QmmError(Timeout) if a kernel gave up a bounded wait."""
     check(lib().qmm_device_status(_stream_handle(stream)))
+
+
+TENSOR_KINDS = {"bf16": 0, "mxf8f6f4": 1, "mxf4nvf4": 2}
+
+
+def tensor_peak(kind: str, iters: int = 1 << 15, stream=None) -> float:
+    """Measured dense tcgen05 rate (TFLOP/s) of one MMA kind on the current
+    device: "bf16" (kind::f16), "mxf8f6f4" (E4M3, UE8M0 per 32) or
+    "mxf4nvf4" (E2M1, UE4M3 per 16)."""
+    out = ctypes.c_double()
+    check(lib().qmm_tensor_peak(TENSOR_KINDS[kind], iters, _stream_handle(stream), ctypes.byref(out)))
+    return out.value
 
 
 def fault_arm(k: int) -> None:
@@ -423,6 +438,22 @@ class QuantizedWeight:
         y = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
         check(lib().qmm_run(self.handle, x2.data_ptr(), m, x2.stride(0), y.data_ptr(), y.stride(0), True,
                             _stream_handle(stream)))
+        return y.reshape(*x.shape[:-1], self.n) if out is None else y
+
+    def run_blockscaled(self, x, out=None, stream=None):
+        """y = quantize_nvfp4(x) . dequant(W)^T on the block-scaled FP4 tensor
+        cores (qmm_run_blockscaled): NOT the parity path - x is quantised."""
+        torch = _torch()
+        if x.dtype != torch.bfloat16:
+            raise QmmError(7, f"x must be bfloat16, got {x.dtype}")
+        _need_cuda("x", x, self.device)
+        x2 = _as_2d(x)
+        m = x2.shape[0]
+        if out is not None:
+            _check_out(out, m, self.n, self.device)
+        y = out if out is not None else torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
+        check(lib().qmm_run_blockscaled(self.handle, x2.data_ptr(), m, x2.stride(0), y.data_ptr(), y.stride(0),
+                                        _stream_handle(stream)))
         return y.reshape(*x.shape[:-1], self.n) if out is None else y
 
     def argmax(self, x, logits: bool = False, stream=None):

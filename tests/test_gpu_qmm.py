@@ -34,8 +34,7 @@ def bits(t):
 
 def check_parity(y_gpu, x, codes, scales, mode, frob=None):
     xb = bits(x)
-    ref = oracle.qmm_f64(xb, codes, scales, mode)
-    absref = oracle.abs_qmm_f64(xb, codes, scales, mode)
+    ref, absref = oracle.qmm_f64_abs(xb, codes, scales, mode)
     y = oracle.bf16_bits_to_f32(bits(y_gpu))
     assert oracle.parity_violations(y, ref, absref) == 0
     rf = oracle.rel_frobenius(y, ref)
