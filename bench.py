@@ -235,6 +235,32 @@ def prefill_measure(args, qmm, dev, world: int, rank: int, barrier, max_over_ran
     tflops = flops / (ms * 1e-3) / 1e12
     peak, kind = bf16_peak()
     per_gpu = 2.0 * m * wt.n * k / (ms * 1e-3) / 1e12
+    # The x-quantised block-scaled variant (qmm_run_blockscaled, FP4 tensor
+    # cores; not the parity path) on the same shard, and its distance from
+    # the exact result above.
+    bs = None
+    try:
+        yb = torch.empty_like(y)
+        for _ in range(max(1, args.prefill_warmup)):
+            wt.run_blockscaled(x, out=yb, stream=stream)
+        barrier()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(args.prefill_steps):
+            wt.run_blockscaled(x, out=yb, stream=stream)
+        b1.record(stream)
+        barrier()
+        bms = max_over_ranks(b0.elapsed_time(b1)) / args.prefill_steps
+        qmm.device_status(stream)
+        rf = float((yb.float() - y.float()).norm() / y.float().norm())
+        bs = {"kernel": "qmm_gemm_bs_kernel (tcgen05.mma kind::mxf4nvf4.block_scale.block16)",
+              "ms_per_gemm": bms, "tflops": flops / (bms * 1e-3) / 1e12,
+              "tflops_per_gpu": 2.0 * m * wt.n * k / (bms * 1e-3) / 1e12,
+              "rel_frobenius_vs_exact": rf,
+              "note": "x quantised to nvfp4 per call (included in the time): NOT the parity path"}
+        del yb
+    except Exception as exc:  # recorded, not raised
+        bs = {"error": repr(exc)}
     wt.close()
     return {"workload": f"cfg3: nvfp4 prefill GEMM x [{m}, {k}] . W[{n}, {k}]^T, N-sharded over {world} GPU(s)",
             "metric": "TFLOP/s", "value": tflops, "ms_per_gemm": ms, "steps": args.prefill_steps,
@@ -243,7 +269,8 @@ def prefill_measure(args, qmm, dev, world: int, rank: int, barrier, max_over_ran
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                          "frac": per_gpu / peak, "peak_kind": kind, "kernel": "qmm_gemm_kernel<nvfp4>",
                          "note": "dense bf16 MMA peak: W is dequantised exactly to bf16 (parity); "
-                                 "the block-scaled FP4 peak (~9 PF nominal) needs x quantised to FP4"}}
+                                 "the block-scaled FP4 peak (~9 PF nominal) needs x quantised to FP4"},
+            "blockscaled": bs}
 
 
 def _rand_nvfp4(n: int, k: int, dev, seed: int):
@@ -1097,6 +1124,9 @@ def main() -> None:
         tp = prefill["roofline"]["achieved"]
         prefill["roofline"]["frac_of_tcgen05_bf16_peak"] = tp / tensor_peaks["bf16"]
         prefill["roofline"]["frac_of_mxf4nvf4_peak"] = tp / tensor_peaks["mxf4nvf4"]
+        bsr = prefill.get("blockscaled") or {}
+        if "tflops_per_gpu" in bsr:
+            bsr["frac_of_mxf4nvf4_peak"] = bsr["tflops_per_gpu"] / tensor_peaks["mxf4nvf4"]
 
     if rank == 0:
         line = {

@@ -56,9 +56,7 @@ __device__ unsigned int g_gemv_tc_error = 0;
 namespace {
 
 constexpr int kRows = 128;                 // rows per unit (8 warps x 16)
-constexpr int kStages = 4;
 constexpr int kBox = kRows * 128;          // one 2D TMA box: 128 rows x 128 code bytes
-constexpr int kCodeBytes = 2 * kBox;       // 32 KB: 256 code bytes per row per unit
 constexpr int kXRows = 8;                  // x rows staged per unit (M padded to 8)
 constexpr int kConverters = 3;             // x-converter warps (tokens m = v, v + 3, v + 6)
 constexpr int kConsumers = 16;             // 8 row groups x 2 k halves
@@ -66,14 +64,22 @@ constexpr int kFirstConsumer = 1 + kConverters;  // warp index of consumer 0
 constexpr int kThreads = (1 + kConverters + kConsumers) * 32;  // producer, converters, consumers
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
+// A unit is 128 rows x kBoxes 128-byte code boxes per row; the ring holds
+// kStages units (about 147 KB of weights in flight either way).  nvfp4 units
+// are one box (256 codes): twice as many units as two-box units, so the
+// stream-K split leaves at most half a two-box unit of imbalance between CTAs.
 template <int FMT> struct Cfg;
 template <> struct Cfg<kMXFP8> {
-    static constexpr int KC = 256;         // codes per row per unit
-    static constexpr int SB = 8;           // scale bytes per row per unit
+    static constexpr int kBoxes = 2;
+    static constexpr int KC = 128 * kBoxes;   // codes per row per unit
+    static constexpr int SB = KC / 32;        // scale bytes per row per unit
+    static constexpr int kStages = 4;
 };
 template <> struct Cfg<kNVFP4> {
-    static constexpr int KC = 512;
-    static constexpr int SB = 32;
+    static constexpr int kBoxes = 1;
+    static constexpr int KC = 256 * kBoxes;
+    static constexpr int SB = KC / 16;
+    static constexpr int kStages = 8 / kBoxes;
 };
 
 struct TcParams {
@@ -238,6 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                                                                    const __grid_constant__ CUtensorMap smap,
                                                                    TcParams p) {
     constexpr int KC = Cfg<FMT>::KC;
+    constexpr int kStages = Cfg<FMT>::kStages;
+    constexpr int kCodeBytes = Cfg<FMT>::kBoxes * kBox;    // one unit's codes
     constexpr int SB = ScaleLayout<FMT, SRC>::kStride;     // bytes per row of a staged scale tile
     constexpr int kScaleBytes = ScaleLayout<FMT, SRC>::kBytes;
     constexpr int kXRawBytes = kXRows * KC * 2;
@@ -294,8 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             auto issue_w = [&](int i) {
                 const int s = i % kStages;
                 mbar_expect_tx(&full[s], kCodeBytes + kScaleBytes);
-                tma_2d(s_codes + s * kCodeBytes, &cmap, &full[s], w_kc * 256, w_rb * kRows);
-                tma_2d(s_codes + s * kCodeBytes + kBox, &cmap, &full[s], w_kc * 256 + 128, w_rb * kRows);
+#pragma unroll
+                for (int b = 0; b < Cfg<FMT>::kBoxes; ++b)
+                    tma_2d(s_codes + s * kCodeBytes + b * kBox, &cmap, &full[s], (w_kc * Cfg<FMT>::kBoxes + b) * 128,
+                           w_rb * kRows);
                 if constexpr (SRC == kScaleCkpt)
                     tma_2d(s_scales + s * kScaleBytes, &smap, &full[s], (w_kc * Cfg<FMT>::SB) & ~15, w_rb * kRows);
                 else
@@ -323,8 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if (p.l2_prefetch) {
                 int f_rb = w_rb, f_kc = w_kc;
                 for (int i = pre; i < nunits; ++i) {
-                    tma_prefetch_2d(&cmap, f_kc * 256, f_rb * kRows);
-                    tma_prefetch_2d(&cmap, f_kc * 256 + 128, f_rb * kRows);
+                    for (int b = 0; b < Cfg<FMT>::kBoxes; ++b)
+                        tma_prefetch_2d(&cmap, (f_kc * Cfg<FMT>::kBoxes + b) * 128, f_rb * kRows);
                     if constexpr (SRC == kScaleCkpt)
                         tma_prefetch_2d(&smap, (f_kc * Cfg<FMT>::SB) & ~15, f_rb * kRows);
                     else
@@ -416,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                     // quad c = (R / 4) % 4, step pair jp = 4 su + R % 4.  The
                     // B-fragment lane is 4 n + c for the run's mma column n.
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const int R = 2 * lane + q, jp = 4 * (R >> 4) + (R & 3), c = (R >> 2) & 3;
+                    for (int q = 0; q < Cfg<FMT>::kBoxes; ++q) {
+                        const int R = Cfg<FMT>::kBoxes * lane + q, jp = 4 * (R >> 4) + (R & 3), c = (R >> 2) & 3;
                         int bl;
                         if constexpr (XL == kXlTokens) bl = 4 * m + c;              // n = m
                         else bl = 9 * c + 4 * m;                                     // n = 2 c + m
@@ -444,13 +454,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         // over one half of the unit's k range (kh = cw / 8).
         const int cw = warp - kFirstConsumer, rg = cw & 7, kh = cw >> 3;
         const int g = lane >> 2, c = lane & 3;
-        const int r0 = 16 * rg + g, r1 = r0 + 8;
-        // B-fragment lane 4 n + c carries x only when its column n holds an x
-        // row < M (kXlGroups2: n = 2 c + t, so only lanes with g / 2 == c and
-        // t < M); the other lanes' slots are zero for the whole launch, so
-        // they skip the shared-memory load (M <= 2 reads 1/8 - 1/4 of the
-        // fragment bytes).
-        const bool x_live = (XL == kXlGroups2 && FMT == kNVFP4) ? ((g >> 1) == c && (g & 1) < p.m) : (g < p.m);
+        // MMA row slot g computes tile row 16 rg + (g >> 1) + 4 (g & 1) (and
+        // that + 8).  A quarter-warp phase of a 16-byte shared load covers
+        // the lanes of two consecutive slots; with the TMA's 128-byte swizzle
+        // (chunk ^= row & 7) rows 4 apart hit disjoint banks, where adjacent
+        // rows would collide on the same 16 (a 2-way conflict on every code
+        // load).  Outputs, scales and partial sums all follow r0 / r1.
+        const int r0 = 16 * rg + ((g >> 1) | ((g & 1) << 2)), r1 = r0 + 8;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
         // Static schedule: CTA j owns units [first_unit(j), first_unit(j + 1));
@@ -806,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         auto consume_groups = [&](const uint8_t* cs, const uint8_t* ss, const uint8_t* xf, float xs0, float xs1) {
             float u[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int si = 0; si < 2; ++si) {
+            for (int si = 0; si < Cfg<FMT>::kBoxes; ++si) {
                 const int su = kh + 2 * si;
                 const uint8_t* cb = cs + (su >> 1) * kBox;
                 const int ch = (4 * su + c) & 7;
@@ -830,8 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
                         const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
                         // da / db: two chains over the step pair's two mmas.
-                        uint4 bx = make_uint4(0u, 0u, 0u, 0u);
-                        if (x_live) bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         mma16816(da, a0, bx.x, bx.y);
                         mma16816(db, a1, bx.z, bx.w);
                     }
@@ -879,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 // mma chains in flight.
                 float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int si = 0; si < 2; ++si) {
+                for (int si = 0; si < Cfg<FMT>::kBoxes; ++si) {
                     const int su = kh + 2 * si;          // this warp's 128-k super-steps of the unit
                     // 16 bytes (32 codes) of rows r0 and r1: box su / 2, chunk
                     // (4 su + c) % 8 of the 128-byte row, 128B-swizzled.
@@ -907,8 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                             ha[b] = hmul2u(ha[b], sa);
                             hb[b] = hmul2u(hb[b], sbv);
                         }
-                        uint4 bx = make_uint4(0u, 0u, 0u, 0u);
-                        if (x_live) bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
+                        const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
                         // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
                         const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
                         const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
@@ -943,8 +951,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         a[1] = e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFF));
                         a[2] = e4m3x2_to_f16x2((uint16_t)(wa >> 16));
                         a[3] = e4m3x2_to_f16x2((uint16_t)(wb >> 16));
-                        uint2 b = make_uint2(0u, 0u);
-                        if (x_live) b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
+                        const uint2 b = *reinterpret_cast<const uint2*>(xf + ((grp * 32 + lane) * 16) + h * 8);
                         mma16816(d, a, b.x, b.y);
                     }
                     const float sc0 = ue8m0_to_f32((sw0 >> (8 * gi)) & 0xFF);
@@ -1002,7 +1009,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 template <int FMT, int SRC = kScaleTiled>
 constexpr int smem_bytes() {
-    return 1024 + kStages * (kCodeBytes + ScaleLayout<FMT, SRC>::kBytes + 2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
+    return 1024 + Cfg<FMT>::kStages * (Cfg<FMT>::kBoxes * kBox + ScaleLayout<FMT, SRC>::kBytes +
+                                       2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
            kRows * 8 * 4 + 512;
 }
 
