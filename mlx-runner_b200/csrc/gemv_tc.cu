@@ -65,9 +65,10 @@ constexpr int kThreads = (1 + kConverters + kConsumers) * 32;  // producer, conv
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 // A unit is 128 rows x kBoxes 128-byte code boxes per row; the ring holds
-// kStages units (about 147 KB of weights in flight either way).  nvfp4 units
-// are one box (256 codes): twice as many units as two-box units, so the
-// stream-K split leaves at most half a two-box unit of imbalance between CTAs.
+// kStages units (about 147 KB of weights in flight).  Two-box units for
+// both formats: one-box nvfp4 units (twice as many, an 8-stage ring) halve
+// the stream-K imbalance between CTAs but measured slower (cfg2 M = 1
+// 15.3 -> 16.6 us): the per-unit barrier and hand-over cost dominates.
 template <int FMT> struct Cfg;
 template <> struct Cfg<kMXFP8> {
     static constexpr int kBoxes = 2;
@@ -76,7 +77,7 @@ template <> struct Cfg<kMXFP8> {
     static constexpr int kStages = 4;
 };
 template <> struct Cfg<kNVFP4> {
-    static constexpr int kBoxes = 1;
+    static constexpr int kBoxes = 2;
     static constexpr int KC = 256 * kBoxes;
     static constexpr int SB = KC / 16;
     static constexpr int kStages = 8 / kBoxes;
