@@ -69,6 +69,12 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;
 // both formats: one-box nvfp4 units (twice as many, an 8-stage ring) halve
 // the stream-K imbalance between CTAs but measured slower (cfg2 M = 1
 // 15.3 -> 16.6 us): the per-unit barrier and hand-over cost dominates.
+// Consumer split of a unit: NKS k slices x (8 / NRG) warps of NRG row groups
+// (16 rows each), NKS * 8 / NRG = 16 warps.  nvfp4 takes kNvSlices k slices;
+// mxfp8 two.  More k slices share each x-fragment load among more row groups
+// per warp, at the cost of a (NKS - 1)-way shared-memory reduction per flush.
+constexpr int kNvSlices = 4;
+
 template <int FMT> struct Cfg;
 template <> struct Cfg<kMXFP8> {
     static constexpr int kBoxes = 2;
@@ -258,8 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     uint8_t* s_xraw = s_scales + kStages * kScaleBytes;               // kStages x kXRawBytes
     uint8_t* s_xf = s_xraw + kStages * kXRawBytes;                    // kStages x kXfBytes
     float* s_xs = reinterpret_cast<float*>(s_xf + kStages * kXfBytes);  // kStages x 8
-    float* s_red = s_xs + kStages * 8;                                  // 128 x 8 (k-half sums)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + kRows * 8);
+    constexpr int NKS = FMT == kNVFP4 ? kNvSlices : 2;    // k slices per unit
+    constexpr int NRG = NKS / 2;                          // row groups per consumer warp
+    float* s_red = s_xs + kStages * 8;                    // (NKS - 1) x 128 x 8 (k-slice sums)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + (NKS - 1) * kRows * 8);
     uint64_t* full = bars;                  // weight tiles (codes + scales) landed
     uint64_t* xready = bars + kStages;      // f16 x fragments written
     uint64_t* empty = bars + 2 * kStages;   // every consumer is done with the stage
@@ -451,9 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         }
     } else {
         // ---------------- consumers ----------------
-        // Warp cw owns rows [16 rg, 16 rg + 16) of every unit (rg = cw % 8)
-        // over one half of the unit's k range (kh = cw / 8).
-        const int cw = warp - kFirstConsumer, rg = cw & 7, kh = cw >> 3;
+        // Warp cw owns row groups rg0 .. rg0 + NRG - 1 (16 rows each) of every
+        // unit over k slice kh of NKS (super-steps kh, kh + NKS, ... of the
+        // unit's 128-code super-steps).
+        const int cw = warp - kFirstConsumer, kh = cw / (8 / NRG), rg0 = (cw % (8 / NRG)) * NRG;
         const int g = lane >> 2, c = lane & 3;
         // MMA row slot g computes tile row 16 rg + (g >> 1) + 4 (g & 1) (and
         // that + 8).  A quarter-warp phase of a 16-byte shared load covers
@@ -461,8 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         // (chunk ^= row & 7) rows 4 apart hit disjoint banks, where adjacent
         // rows would collide on the same 16 (a 2-way conflict on every code
         // load).  Outputs, scales and partial sums all follow r0 / r1.
-        const int r0 = 16 * rg + ((g >> 1) | ((g & 1) << 2)), r1 = r0 + 8;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int r0[NRG], r1[NRG];
+#pragma unroll
+        for (int j = 0; j < NRG; ++j) {
+            r0[j] = 16 * (rg0 + j) + ((g >> 1) | ((g & 1) << 2));
+            r1[j] = r0[j] + 8;
+        }
+        float acc[NRG][4];
+#pragma unroll
+        for (int j = 0; j < NRG; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
         // Static schedule: CTA j owns units [first_unit(j), first_unit(j + 1));
         // unit u belongs to CTA owner(u).  32-bit division when the products
@@ -753,29 +769,43 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 // Lanes c of a quad hold x rows 0, 1 over group slot c: add the
                 // slots (fixed butterfly order); lane c = 0 then holds columns 0, 1.
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 1);
-                    acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], 2);
-                    if (c != 0) acc[i] = 0.f;
-                }
+                for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[j][i] += __shfl_xor_sync(0xFFFFFFFFu, acc[j][i], 1);
+                        acc[j][i] += __shfl_xor_sync(0xFFFFFFFFu, acc[j][i], 2);
+                        if (c != 0) acc[j][i] = 0.f;
+                    }
             }
             // rows r0 / r1 of block rb, x rows (columns) 2c, 2c + 1.  The k
-            // half kh = 1 hands its sums to kh = 0, which adds them (fixed order).
-            if (kh == 1) {
+            // slices kh > 0 hand their sums to kh = 0, which adds them in
+            // slice order (fixed order).
+            auto red_at = [&](int j, int i) { return (i < 2 ? r0[j] : r1[j]) * 8 + 2 * c + (i & 1); };
+            if (kh > 0) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+                for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) s_red[(kh - 1) * kRows * 8 + red_at(j, i)] = acc[j][i];
             }
             named_sync(1, kConsumers * 32);
             if (kh == 0) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) acc[i] += s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)];
+                for (int q = 1; q < NKS; ++q)
+#pragma unroll
+                    for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) acc[j][i] += s_red[(q - 1) * kRows * 8 + red_at(j, i)];
             }
             constexpr bool to_smem = EPI != kEpiPlain;
             if (complete && to_smem) {
-                // Each kh = 0 thread rewrites the s_red entries it just read.
+                // The kh = 0 threads rewrite slice 1's entries (each its own)
+                // with the final sums: s_red[0 .. 1023] is then the block's
+                // [128 rows][8].
                 if (kh == 0) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) s_red[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+                    for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) s_red[red_at(j, i)] = acc[j][i];
                 }
                 named_sync(1, kConsumers * 32);
                 if constexpr (EPI == kEpiSwiglu) swiglu_out(rb);
@@ -790,13 +820,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if (complete) {
                 if (kh == 0) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int row = rb * kRows + (i < 2 ? r0 : r1), col = 2 * c + (i & 1);
-                        if (row < p.n && col < p.m) {
-                            if (p.yf) p.yf[(int64_t)col * p.ldy + row] = acc[i];
-                            else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[i]);
+                    for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int row = rb * kRows + (i < 2 ? r0[j] : r1[j]), col = 2 * c + (i & 1);
+                            if (row < p.n && col < p.m) {
+                                if (p.yf) p.yf[(int64_t)col * p.ldy + row] = acc[j][i];
+                                else p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(acc[j][i]);
+                            }
                         }
-                    }
                 }
                 named_sync(1, kConsumers * 32);   // s_red is reused by the next flush
                 return;
@@ -805,7 +837,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             float* part = p.partial + ((int64_t)blockIdx.x * 2 + slot) * kRows * 8;
             if (kh == 0) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) part[(i < 2 ? r0 : r1) * 8 + 2 * c + (i & 1)] = acc[i];
+                for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) part[red_at(j, i)] = acc[j][i];
             }
             arrive_partial(rb);
         };
@@ -815,47 +849,68 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
         // accumulators whose column 2c + t is group slot c of x row t, which
         // the group scales of rows r0 / r1 then weight in fp32.
         auto consume_groups = [&](const uint8_t* cs, const uint8_t* ss, const uint8_t* xf, float xs0, float xs1) {
-            float u[4] = {0.f, 0.f, 0.f, 0.f};
+            float u[NRG][4];
 #pragma unroll
-            for (int si = 0; si < Cfg<FMT>::kBoxes; ++si) {
-                const int su = kh + 2 * si;
+            for (int j = 0; j < NRG; ++j) u[j][0] = u[j][1] = u[j][2] = u[j][3] = 0.f;
+#pragma unroll
+            for (int si = 0; si < 2 * Cfg<FMT>::kBoxes / NKS; ++si) {
+                const int su = kh + NKS * si;
                 const uint8_t* cb = cs + (su >> 1) * kBox;
                 const int ch = (4 * su + c) & 7;
-                const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0 * 128 + ((ch ^ (r0 & 7)) << 4));
-                const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1 * 128 + ((ch ^ (r1 & 7)) << 4));
-                // Scales of group slot c (its two halves) for rows r0 and r1.
-                const float2 sa0 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c)));
-                const float2 sa1 = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c)));
-                const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+                uint32_t wa[NRG][4], wb[NRG][4];
+                float2 sa0[NRG], sa1[NRG];
+#pragma unroll
+                for (int j = 0; j < NRG; ++j) {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0[j] * 128 + ((ch ^ (r0[j] & 7)) << 4));
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1[j] * 128 + ((ch ^ (r1[j] & 7)) << 4));
+                    wa[j][0] = w0.x; wa[j][1] = w0.y; wa[j][2] = w0.z; wa[j][3] = w0.w;
+                    wb[j][0] = w1.x; wb[j][1] = w1.y; wb[j][2] = w1.z; wb[j][3] = w1.w;
+                    // Scales of group slot c (its two halves) for rows r0 and r1.
+                    sa0[j] = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r0[j] * SB + 8 * su + 2 * c)));
+                    sa1[j] = f16x2_to_float2(e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(ss + r1[j] * SB + 8 * su + 2 * c)));
+                }
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
-                    float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+                    float da[NRG][4], db[NRG][4];
+#pragma unroll
+                    for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) da[j][i] = db[j][i] = 0.f;
 #pragma unroll
                     for (int jq = 0; jq < 2; ++jq) {
                         const int jp = 2 * half + jq;
-                        // Word jp of rows r0 / r1 (8 codes each) widened just
-                        // before its mmas: 8 live f16 pairs instead of 32.
-                        uint32_t ha[4], hb[4];
-                        e2m1x8_to_f16x2(wa[jp], ha);
-                        e2m1x8_to_f16x2(wb[jp], hb);
-                        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
-                        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
-                        // da / db: two chains over the step pair's two mmas.
+                        // One x-fragment load feeds every row group of the warp.
                         const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
-                        mma16816(da, a0, bx.x, bx.y);
-                        mma16816(db, a1, bx.z, bx.w);
+#pragma unroll
+                        for (int j = 0; j < NRG; ++j) {
+                            // Word jp of rows r0 / r1 (8 codes each) widened just
+                            // before its mmas: 8 live f16 pairs instead of 32.
+                            uint32_t ha[4], hb[4];
+                            e2m1x8_to_f16x2(wa[j][jp], ha);
+                            e2m1x8_to_f16x2(wb[j][jp], hb);
+                            const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
+                            const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
+                            mma16816(da[j], a0, bx.x, bx.y);
+                            mma16816(db[j], a1, bx.z, bx.w);
+                        }
                     }
-                    const float fa0 = half ? sa0.y : sa0.x, fa1 = half ? sa1.y : sa1.x;
-                    u[0] = fmaf(da[0] + db[0], fa0, u[0]);
-                    u[1] = fmaf(da[1] + db[1], fa0, u[1]);
-                    u[2] = fmaf(da[2] + db[2], fa1, u[2]);
-                    u[3] = fmaf(da[3] + db[3], fa1, u[3]);
+#pragma unroll
+                    for (int j = 0; j < NRG; ++j) {
+                        const float fa0 = half ? sa0[j].y : sa0[j].x, fa1 = half ? sa1[j].y : sa1[j].x;
+                        u[j][0] = fmaf(da[j][0] + db[j][0], fa0, u[j][0]);
+                        u[j][1] = fmaf(da[j][1] + db[j][1], fa0, u[j][1]);
+                        u[j][2] = fmaf(da[j][2] + db[j][2], fa1, u[j][2]);
+                        u[j][3] = fmaf(da[j][3] + db[j][3], fa1, u[j][3]);
+                    }
                 }
             }
-            acc[0] = fmaf(u[0], xs0, acc[0]);
-            acc[1] = fmaf(u[1], xs1, acc[1]);
-            acc[2] = fmaf(u[2], xs0, acc[2]);
-            acc[3] = fmaf(u[3], xs1, acc[3]);
+#pragma unroll
+            for (int j = 0; j < NRG; ++j) {
+                acc[j][0] = fmaf(u[j][0], xs0, acc[j][0]);
+                acc[j][1] = fmaf(u[j][1], xs1, acc[j][1]);
+                acc[j][2] = fmaf(u[j][2], xs0, acc[j][2]);
+                acc[j][3] = fmaf(u[j][3], xs1, acc[j][3]);
+            }
         };
         int next_rb = u0 / p.kchunks, next_kc = u0 - next_rb * p.kchunks;   // advanced per unit
         for (int i = 0; i < nunits; ++i) {
@@ -866,7 +921,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                 cur_rb = rb;
                 if (first_rb < 0) first_rb = rb;
                 rb_first_unit = kc;
-                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+                for (int j = 0; j < NRG; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
             }
             const int s = i % kStages;
             const uint32_t ph = (uint32_t)(i / kStages) & 1u;
@@ -885,56 +941,71 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if constexpr (FMT == kNVFP4 && XL != kXlTokens) {
                 consume_groups(cs, ss, xf, xs0, xs1);
             } else if constexpr (FMT == kNVFP4) {
-                // Two accumulators (first / second mma of each word) keep two
-                // mma chains in flight.
-                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+                // Two accumulators per row group (first / second mma of each
+                // word) keep two mma chains in flight per row group.
+                float d0[NRG][4], d1[NRG][4];
 #pragma unroll
-                for (int si = 0; si < Cfg<FMT>::kBoxes; ++si) {
-                    const int su = kh + 2 * si;          // this warp's 128-k super-steps of the unit
+                for (int j = 0; j < NRG; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) d0[j][i] = d1[j][i] = 0.f;
+#pragma unroll
+                for (int si = 0; si < 2 * Cfg<FMT>::kBoxes / NKS; ++si) {
+                    const int su = kh + NKS * si;        // this warp's 128-k super-steps of the unit
                     // 16 bytes (32 codes) of rows r0 and r1: box su / 2, chunk
                     // (4 su + c) % 8 of the 128-byte row, 128B-swizzled.
                     const uint8_t* cb = cs + (su >> 1) * kBox;
                     const int ch = (4 * su + c) & 7;
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0 * 128 + ((ch ^ (r0 & 7)) << 4));
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1 * 128 + ((ch ^ (r1 & 7)) << 4));
-                    // Scales: 2 groups of 16 codes per row.
-                    const uint32_t sb0 = *reinterpret_cast<const uint16_t*>(ss + r0 * SB + 8 * su + 2 * c);
-                    const uint32_t sb1 = *reinterpret_cast<const uint16_t*>(ss + r1 * SB + 8 * su + 2 * c);
-                    const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)sb0), s1 = e4m3x2_to_f16x2((uint16_t)sb1);
-                    const uint32_t s0lo = __byte_perm(s0, 0, 0x1010), s0hi = __byte_perm(s0, 0, 0x3232);
-                    const uint32_t s1lo = __byte_perm(s1, 0, 0x1010), s1hi = __byte_perm(s1, 0, 0x3232);
-                    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+                    uint32_t wa[NRG][4], wb[NRG][4], slo[NRG][2], shi[NRG][2];
+#pragma unroll
+                    for (int j = 0; j < NRG; ++j) {
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(cb + r0[j] * 128 + ((ch ^ (r0[j] & 7)) << 4));
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(cb + r1[j] * 128 + ((ch ^ (r1[j] & 7)) << 4));
+                        wa[j][0] = w0.x; wa[j][1] = w0.y; wa[j][2] = w0.z; wa[j][3] = w0.w;
+                        wb[j][0] = w1.x; wb[j][1] = w1.y; wb[j][2] = w1.z; wb[j][3] = w1.w;
+                        // Scales: 2 groups of 16 codes per row.
+                        const uint32_t sb0 = *reinterpret_cast<const uint16_t*>(ss + r0[j] * SB + 8 * su + 2 * c);
+                        const uint32_t sb1 = *reinterpret_cast<const uint16_t*>(ss + r1[j] * SB + 8 * su + 2 * c);
+                        const uint32_t s0 = e4m3x2_to_f16x2((uint16_t)sb0), s1 = e4m3x2_to_f16x2((uint16_t)sb1);
+                        slo[j][0] = __byte_perm(s0, 0, 0x1010); shi[j][0] = __byte_perm(s0, 0, 0x3232);
+                        slo[j][1] = __byte_perm(s1, 0, 0x1010); shi[j][1] = __byte_perm(s1, 0, 0x3232);
+                    }
 #pragma unroll
                     for (int jp = 0; jp < 4; ++jp) {
-                        // Word jp of rows r0 / r1 widened and scaled just before
-                        // its mmas: ha[b] = f16x2 of byte 4 jp + b (codes 2b, 2b + 1).
-                        uint32_t ha[4], hb[4];
-                        e2m1x8_to_f16x2(wa[jp], ha);
-                        e2m1x8_to_f16x2(wb[jp], hb);
-                        const uint32_t sa = jp < 2 ? s0lo : s0hi, sbv = jp < 2 ? s1lo : s1hi;
-#pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            ha[b] = hmul2u(ha[b], sa);
-                            hb[b] = hmul2u(hb[b], sbv);
-                        }
                         const uint4 bx = *reinterpret_cast<const uint4*>(xf + ((su * 4 + jp) * 32 + lane) * 16);
-                        // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
-                        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
-                        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
-                        mma16816(d0, a0, bx.x, bx.y);
-                        mma16816(d1, a1, bx.z, bx.w);
+#pragma unroll
+                        for (int j = 0; j < NRG; ++j) {
+                            // Word jp of rows r0 / r1 widened and scaled just before
+                            // its mmas: ha[b] = f16x2 of byte 4 jp + b (codes 2b, 2b + 1).
+                            uint32_t ha[4], hb[4];
+                            e2m1x8_to_f16x2(wa[j][jp], ha);
+                            e2m1x8_to_f16x2(wb[j][jp], hb);
+                            const uint32_t sa = jp < 2 ? slo[j][0] : shi[j][0], sbv = jp < 2 ? slo[j][1] : shi[j][1];
+#pragma unroll
+                            for (int b2 = 0; b2 < 4; ++b2) {
+                                ha[b2] = hmul2u(ha[b2], sa);
+                                hb[b2] = hmul2u(hb[b2], sbv);
+                            }
+                            // step j = 2 jp + jj uses bytes 2j (codes 4j, 4j+1) and 2j + 1.
+                            const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
+                            const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
+                            mma16816(d0[j], a0, bx.x, bx.y);
+                            mma16816(d1[j], a1, bx.z, bx.w);
+                        }
                     }
                 }
-                acc[0] = fmaf(d0[0] + d1[0], xs0, acc[0]);
-                acc[1] = fmaf(d0[1] + d1[1], xs1, acc[1]);
-                acc[2] = fmaf(d0[2] + d1[2], xs0, acc[2]);
-                acc[3] = fmaf(d0[3] + d1[3], xs1, acc[3]);
+#pragma unroll
+                for (int j = 0; j < NRG; ++j) {
+                    acc[j][0] = fmaf(d0[j][0] + d1[j][0], xs0, acc[j][0]);
+                    acc[j][1] = fmaf(d0[j][1] + d1[j][1], xs1, acc[j][1]);
+                    acc[j][2] = fmaf(d0[j][2] + d1[j][2], xs0, acc[j][2]);
+                    acc[j][3] = fmaf(d0[j][3] + d1[j][3], xs1, acc[j][3]);
+                }
             } else {
                 // mxfp8: step j covers k [16j, 16j + 16) (one half group);
                 // thread c owns bytes 16j + 4c .. + 3 of each row.
                 const int soff = (SRC == kScaleCkpt) ? (kc & 1) * 8 : 0;   // the unit's 8 bytes in a 16-byte box row
-                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0 * SB + soff + 4 * kh);
-                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1 * SB + soff + 4 * kh);
+                const uint32_t sw0 = *reinterpret_cast<const uint32_t*>(ss + r0[0] * SB + soff + 4 * kh);
+                const uint32_t sw1 = *reinterpret_cast<const uint32_t*>(ss + r1[0] * SB + soff + 4 * kh);
 #pragma unroll
                 for (int gi = 0; gi < 4; ++gi) {
                     const int grp = 4 * kh + gi;         // this warp's four 32-code groups
@@ -944,9 +1015,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                         const int j = 2 * grp + h;
                         const uint8_t* cb = cs + (j >> 3) * kBox;
                         const uint32_t wa = *reinterpret_cast<const uint32_t*>(
-                            cb + r0 * 128 + (((j & 7) ^ (r0 & 7)) << 4) + 4 * c);
+                            cb + r0[0] * 128 + (((j & 7) ^ (r0[0] & 7)) << 4) + 4 * c);
                         const uint32_t wb = *reinterpret_cast<const uint32_t*>(
-                            cb + r1 * 128 + (((j & 7) ^ (r1 & 7)) << 4) + 4 * c);
+                            cb + r1[0] * 128 + (((j & 7) ^ (r1[0] & 7)) << 4) + 4 * c);
                         uint32_t a[4];
                         a[0] = e4m3x2_to_f16x2((uint16_t)(wa & 0xFFFF));
                         a[1] = e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFF));
@@ -957,10 +1028,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
                     }
                     const float sc0 = ue8m0_to_f32((sw0 >> (8 * gi)) & 0xFF);
                     const float sc1 = ue8m0_to_f32((sw1 >> (8 * gi)) & 0xFF);
-                    acc[0] = fmaf(d[0], sc0 * xs0, acc[0]);
-                    acc[1] = fmaf(d[1], sc0 * xs1, acc[1]);
-                    acc[2] = fmaf(d[2], sc1 * xs0, acc[2]);
-                    acc[3] = fmaf(d[3], sc1 * xs1, acc[3]);
+                    acc[0][0] = fmaf(d[0], sc0 * xs0, acc[0][0]);
+                    acc[0][1] = fmaf(d[1], sc0 * xs1, acc[0][1]);
+                    acc[0][2] = fmaf(d[2], sc1 * xs0, acc[0][2]);
+                    acc[0][3] = fmaf(d[3], sc1 * xs1, acc[0][3]);
                 }
             }
             }  // live
@@ -1012,7 +1083,7 @@ template <int FMT, int SRC = kScaleTiled>
 constexpr int smem_bytes() {
     return 1024 + Cfg<FMT>::kStages * (Cfg<FMT>::kBoxes * kBox + ScaleLayout<FMT, SRC>::kBytes +
                                        2 * kXRows * Cfg<FMT>::KC * 2 + 8 * 4) +
-           kRows * 8 * 4 + 512;
+           ((FMT == kNVFP4 ? kNvSlices : 2) - 1) * kRows * 8 * 4 + 512;
 }
 
 using GemvTcKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcParams);
