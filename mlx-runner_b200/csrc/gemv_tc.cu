@@ -72,8 +72,10 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;
 // Consumer split of a unit: NKS k slices x (8 / NRG) warps of NRG row groups
 // (16 rows each), NKS * 8 / NRG = 16 warps.  nvfp4 takes kNvSlices k slices;
 // mxfp8 two.  More k slices share each x-fragment load among more row groups
-// per warp, at the cost of a (NKS - 1)-way shared-memory reduction per flush.
-constexpr int kNvSlices = 4;
+// per warp, at the cost of a (NKS - 1)-way shared-memory reduction per flush
+// and twice the code registers per warp: four slices measured slower than two
+// (cfg2 M = 1 15.4 -> 15.9 us, the lm_head 132 -> 141 us).
+constexpr int kNvSlices = 2;
 
 template <int FMT> struct Cfg;
 template <> struct Cfg<kMXFP8> {
