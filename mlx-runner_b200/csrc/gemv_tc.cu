@@ -100,6 +100,7 @@ struct TcParams {
     int64_t ldy;
     int m, n, k;
     int kchunks, row_blocks, units;
+    int gap;                                   // empty schedule slots after each row block (flush_slots)
     // > 0: gate / up rows interleaved in 64-row blocks; y gets silu(g) * u
     // for swiglu_n columns (row block rb -> columns [64 rb, 64 rb + 64)).
     int swiglu_n;
@@ -282,8 +283,30 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     volatile int* s_tp_list = abort_flag + 4;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int u0 = (int)(((int64_t)p.units * blockIdx.x) / gridDim.x);
-    const int u1 = (int)(((int64_t)p.units * (blockIdx.x + 1)) / gridDim.x);
+    // Static schedule over slots: each row block is its kchunks units then
+    // p.gap empty slots (the cost of the flush that follows it), and CTA j
+    // owns slots [V j / G, V (j + 1) / G), i.e. the units in them.  A CTA
+    // whose range holds a row-block boundary therefore takes fewer units.
+    // Unit u belongs to CTA owner(u).  32-bit division when the products fit
+    // (64-bit division is a long software sequence).
+    const unsigned G = gridDim.x;
+    const int kcg = p.kchunks + p.gap;
+    const int64_t V = (int64_t)p.row_blocks * kcg;
+    const bool fits32 = (uint64_t)(V + 1) * G < (1ull << 32);
+    auto unit_of_slot = [&](int64_t v) -> int {          // first unit at or after slot v
+        if (p.gap == 0) return (int)v;
+        const unsigned rb = (unsigned)v / (unsigned)kcg, o = (unsigned)v - rb * (unsigned)kcg;
+        return (int)(rb * (unsigned)p.kchunks + min(o, (unsigned)p.kchunks));
+    };
+    auto first_unit = [&](int j) -> int {
+        return unit_of_slot(fits32 ? (int64_t)(((unsigned)V * (unsigned)j) / G) : (V * j) / G);
+    };
+    auto owner = [&](int u) -> int {
+        const int64_t v = p.gap == 0 ? u : (int64_t)(u / p.kchunks) * kcg + u % p.kchunks;
+        return fits32 ? (int)(((unsigned)(v + 1) * G - 1u) / (unsigned)V) : (int)(((v + 1) * G - 1) / V);
+    };
+    const int u0 = first_unit((int)blockIdx.x);
+    const int u1 = first_unit((int)blockIdx.x + 1);
     const int nunits = u1 - u0;
 
     if (threadIdx.x == 0) {
@@ -482,18 +505,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
 #pragma unroll
         for (int j = 0; j < NRG; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
         int cur_rb = -1, first_rb = -1, rb_first_unit = 0;
-        // Static schedule: CTA j owns units [first_unit(j), first_unit(j + 1));
-        // unit u belongs to CTA owner(u).  32-bit division when the products
-        // fit (64-bit division is a long software sequence).
-        const unsigned G = gridDim.x;
-        const bool fits32 = (uint64_t)(p.units + 1) * G < (1ull << 32);
-        auto first_unit = [&](int j) -> int {
-            return fits32 ? (int)(((unsigned)p.units * (unsigned)j) / G) : (int)(((int64_t)p.units * j) / G);
-        };
-        auto owner = [&](int u) -> int {
-            return fits32 ? (int)(((unsigned)(u + 1) * G - 1u) / (unsigned)p.units)
-                          : (int)(((int64_t)(u + 1) * G - 1) / p.units);
-        };
         // Row-parallel exchange of row block rb (final fp32 sums in s_red,
         // [128 rows][8 columns]).  tp_push writes them to this rank's slot of
         // every rank's receive buffer and one thread releases them with a
@@ -1100,6 +1111,18 @@ int l2_prefetch_enabled() {
     return on;
 }
 
+// Empty schedule slots after each row block (TcParams::gap).  A CTA whose
+// unit range holds a row-block boundary flushes that block mid-stream (the
+// k-slice hand-over, the partial write and the counter step), which costs
+// about one unit's time while the other CTAs stream on; counting it as
+// kFlushSlots units gives those CTAs that many fewer units.  Off when a CTA
+// would own fewer than kFlushSlots + 2 slots: a shorter range could then
+// lie entirely in a gap and own no unit.
+constexpr int kFlushSlots = 1;
+int flush_slots(int64_t units, int64_t row_blocks, int64_t grid) {
+    return units + row_blocks * kFlushSlots >= grid * (kFlushSlots + 2) ? kFlushSlots : 0;
+}
+
 // Kernel for a format, M, epilogue and scale source, with its dynamic shared
 // memory configured once per device.  nvfp4 takes the group-slot x layout
 // for M <= 2 (the scale leaves the per-code path); QMM_XL=0 keeps the token
@@ -1299,6 +1322,7 @@ int launch_gemv_tc(const qmm_weight* w, const QmmArgs& a, cudaStream_t stream, b
     p.kchunks = st->kchunks;
     p.row_blocks = st->row_blocks;
     p.units = st->kchunks * st->row_blocks;
+    p.gap = flush_slots(p.units, p.row_blocks, st->grid);
     // Programmatic dependent launch: the kernel may start while the previous
     // kernel on the stream finishes; it streams its first weight tiles, then
     // waits (griddepcontrol.wait) before reading x or writing anything.
@@ -1440,6 +1464,7 @@ int launch_gemv_tc_static(const QmmArgs& a, cudaStream_t stream, bool* handled) 
     p.kchunks = (int)kchunks;
     p.row_blocks = (int)row_blocks;
     p.units = (int)units;
+    p.gap = flush_slots(units, row_blocks, grid);
     GemvTcKernel fn = nullptr;
     int smem = 0;
     if (int rc = pick_kernel(fmt, a.m, kEpiPlain, kScaleTiled, dev, &fn, &smem)) return rc;
@@ -1591,6 +1616,7 @@ int launch_gemv_tc_ckpt(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     p.kchunks = (int)kchunks;
     p.row_blocks = (int)row_blocks;
     p.units = (int)units;
+    p.gap = flush_slots(units, row_blocks, grid);
     GemvTcKernel fn = nullptr;
     int smem = 0;
     if (int rc = pick_kernel(fmt, a.m, kEpiPlain, kScaleCkpt, dev, &fn, &smem)) return rc;
