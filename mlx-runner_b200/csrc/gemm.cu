@@ -13,28 +13,37 @@
 //
 // The expensive step is the dequantisation (the fp8/fp4 -> f16 conversions
 // run at a quarter of the fp32 rate on sm_100), so the tile is shaped to
-// dequantise each code once per 512 tokens: one CTA per SM (persistent)
-// computes y^T tiles of 128 weight rows x 512 tokens.  Per 32-wide k-block
-// the dequantised W tile is the A operand (M = 128) of two MMAs whose B
-// operands are the two 256-token halves of the x tile, accumulating into the
-// two 256-column halves of TMEM.  Warp roles (24 warps):
-//   warp 0      TMA producer: x tiles [2 x 256 tokens x 32 k], 64B swizzle
-//   warp 1      MMA issuer: 2 k16 steps x 2 halves of tcgen05.mma kind::f16
-//   warp 2      TMEM allocator (512 columns: one 128 x 512 fp32 tile)
-//   warp 3      TMA producer: W code tiles [128 rows x 32 k]
+// dequantise each code once per 512 tokens, and x - re-read from L2 by every
+// weight tile - is split across a CTA pair.  Two CTAs of a cluster (one per
+// SM, persistent) compute y^T tiles of 256 weight rows x 512 tokens with
+// tcgen05.mma.cta_group::2: per 32-wide k-block, each CTA dequantises its
+// own 128 weight rows (its half of the M = 256 A operand) and loads its
+// 128-token half of each of the two 256-token B operands, so a CTA moves
+// 16 KB of x per k-block instead of 32 KB.  The pair's leader (cluster rank
+// 0) issues two MMAs of 256 x 256 x 16 per k16 step; each CTA's TMEM holds
+// its 128 rows x 512 tokens in fp32 (all 512 columns).  Warp roles (24
+// warps, both CTAs):
+//   warp 0      TMA producer: this CTA's x halves [2 x 128 tokens x 32 k],
+//               64B swizzle, counted on the leader's full_x barrier
+//   warp 1      MMA issuer (leader only): tcgen05.mma.cta_group::2 kind::f16
+//   warp 2      TMEM allocator (512 columns in each CTA, cta_group::2)
+//   warp 3      TMA producer: W code tiles [128 rows x 32 k] (own ring)
 //   warps 4-7   epilogue: tcgen05.ld -> bf16 -> y (coalesced 64-byte rows)
 //   warps 8-23  dequant: 8 codes per thread per k-block from the code ring,
 //               scale bytes prefetched from global memory, decoded with
 //               cvt.{e4m3x2,e2m1x2}, written as bf16 into the A tile in the
 //               UMMA K-major 64B-swizzle layout
-// Pipelines (mbarriers): kStages stages of {x tile, W tile}: full_x (TMA
-// bytes), full_w (16 dequant warps), empty (MMA commit); code tiles: cfull
-// (TMA bytes), cempty (16 dequant warps); accumulator: tmem_full (MMA
-// commit), tmem_empty (4 epilogue warps).  TMA / dequant keep prefetching the
-// next tile while the epilogue drains the accumulator.  Every wait is bounded
-// by %globaltimer: a wait that gives up raises the CTA's abort flag and the
-// device error word, and every role then drains its in-flight TMA / MMA work,
-// frees TMEM and returns (the host reads the word with qmm_device_status).
+// Pipelines (mbarriers): kStages stages of {x halves, W tile}.  On the
+// leader: full_x (both CTAs' TMA bytes), full_w (both CTAs' 16 dequant
+// warps), tmem_empty (both CTAs' 4 epilogue warps).  In each CTA: empty and
+// tmem_full (the leader's MMA commits, one per CTA), and the code ring's
+// cfull (TMA bytes) / cempty (16 dequant warps).  TMA / dequant keep
+// prefetching the next tile while the epilogue drains the accumulator.
+// Every wait is bounded by %globaltimer: a wait that gives up raises the
+// CTA's abort flag and the device error word, every role then drains its
+// in-flight TMA / MMA work, and the pair meets at a cluster barrier before
+// TMEM is freed (the host reads the word with qmm_device_status).  No load
+// uses cluster multicast.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -52,14 +61,16 @@ __device__ unsigned int g_device_error = 0;
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 7;
 constexpr int kBK = 32;                     // k per stage (64 bytes of bf16: one 64B swizzle row)
-constexpr int kTileW = 128;                 // weight rows per tile (MMA M)
+constexpr int kTileW = 128;                 // weight rows per CTA (half the pair's MMA M)
+constexpr int kPairW = 2 * kTileW;          // weight rows per pair tile (MMA M)
 constexpr int kHalfT = 256;                 // tokens per MMA (MMA N)
 constexpr int kTileT = 2 * kHalfT;          // tokens per tile
+constexpr int kCtaT = kHalfT / 2;           // tokens of one MMA's B operand held by each CTA
 constexpr int kThreads = 768;
-constexpr int kXHalfBytes = kHalfT * kBK * 2;   // 16 KB
-constexpr int kXBytes = 2 * kXHalfBytes;        // 32 KB
+constexpr int kXHalfBytes = kCtaT * kBK * 2;    // 8 KB
+constexpr int kXBytes = 2 * kXHalfBytes;        // 16 KB per CTA per stage
 constexpr int kWBytes = kTileW * kBK * 2;       // 8 KB
 constexpr int kCodeRingBytes = 32768;
 // SwiGLU epilogue: a gate-row warp and its up-row warp swap half of each
@@ -152,17 +163,59 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(y0), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// ---- CTA pair (cluster of 2) ------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Shared::cluster address of this CTA's object `p` as it lies in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+// Arrive on a barrier of either CTA of the pair (cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// x half into this CTA's shared memory, the bytes counted on the leader's
+// barrier (cluster address `lead_bar`).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t lead_bar, int x0, int y0) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(y0), "r"(lead_bar)
+        : "memory");
+}
+// One MMA of the pair: D (each CTA's TMEM, its 128 rows) += A (each CTA's
+// 128 rows) x B (each CTA's half of the N columns).  Issued by the leader.
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar)) : "memory");
+// Arrive on barrier `caddr` (cluster address, either CTA) when every pair
+// MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t caddr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(caddr) : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -191,9 +244,9 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
 }
 
 // kind::f16 instruction descriptor: bf16 A/B, fp32 D, K-major A and B,
-// M = 128, N = 256.
+// M = 256 (the pair), N = 256.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kHalfT >> 3) << 17) |
-                            ((uint32_t)(kTileW >> 4) << 24);
+                            ((uint32_t)(kPairW >> 4) << 24);
 
 // ---- W code tiles --------------------------------------------------------------
 // [128 rows x 32 k] per k-block, by TMA into their own ring: 32 bytes per row
@@ -276,16 +329,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
     constexpr int kCBytes = kTileW * CodeTile<FMT>::kRowBytes;   // one code tile
     constexpr int kCStages = kCodeRingBytes / kCBytes;
     extern __shared__ uint8_t smem_raw[];
+    // Both CTAs of the pair carve the same layout from the same aligned base,
+    // so one shared-memory offset names a tile in either CTA (the pair MMA
+    // reads A and B at the leader's descriptor offsets in both).
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* smem_x = smem;                                   // kStages x 32 KB
+    uint8_t* smem_x = smem;                                   // kStages x 16 KB
     uint8_t* smem_w = smem + kStages * kXBytes;               // kStages x 8 KB
     uint8_t* smem_c = smem_w + kStages * kWBytes;             // kCStages code tiles (32 KB)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem_c + kCodeRingBytes);
-    uint64_t* full_x = bars;
-    uint64_t* full_w = bars + kStages;
-    uint64_t* empty = bars + 2 * kStages;
-    uint64_t* tmem_full = bars + 3 * kStages;
-    uint64_t* tmem_empty = tmem_full + 1;
+    uint64_t* full_x = bars;                                  // leader: both CTAs' x bytes
+    uint64_t* full_w = bars + kStages;                        // leader: both CTAs' dequant warps
+    uint64_t* empty = bars + 2 * kStages;                     // each CTA: MMA commit
+    uint64_t* tmem_full = bars + 3 * kStages;                 // each CTA: MMA commit
+    uint64_t* tmem_empty = tmem_full + 1;                     // leader: both CTAs' epilogue warps
     uint64_t* drain = tmem_empty + 1;
     uint64_t* cfull = drain + 1;                              // kCStages
     uint64_t* cempty = cfull + kCStages;                      // kCStages
@@ -300,11 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
     static_assert(kCStages * kCBytes == kCodeRingBytes && kCStages <= 16, "code ring size");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();                     // 0: leader (issues the MMAs)
+    const int pair = (int)cluster_id(), npairs = (int)cluster_count();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_x[s], 1);
-            mbar_init(&full_w[s], kDequantWarps);
+            mbar_init(&full_w[s], 2 * kDequantWarps);
             mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < kCStages; ++s) {
@@ -312,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             mbar_init(&cempty[s], kDequantWarps);
         }
         mbar_init(tmem_full, 1);
-        mbar_init(tmem_empty, kEpiWarps);
+        mbar_init(tmem_empty, 2 * kEpiWarps);
         mbar_init(drain, 1);
         mbar_init(xch_full, kEpiWarps);
         mbar_init(xch_empty, kEpiWarps);
@@ -320,33 +378,39 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         fence_barrier_init();
     }
     if (warp == 2) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;"
                      ::"r"(smem_u32(tmem_base_slot)) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
         tc_fence_before();
     }
+    // Both CTAs' barriers are initialised and their TMEM allocated before
+    // either CTA signals the other.
     __syncthreads();
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_base_slot;
 
-    const int my_tiles = p.num_tiles > (int)blockIdx.x
-                             ? (p.num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int my_tiles = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
     const int total_kb = my_tiles * p.kblocks;
+    // Weight rows of this CTA's half of tile t; first token of tile t.
+    auto w_row0 = [&](int t) { return (t % p.w_tiles) * kPairW + (int)rank * kTileW; };
+    auto tok_0 = [&](int t) { return (t / p.w_tiles) * kTileT; };
 
     if (warp == 0) {
-        // ---------------- TMA producer (x tiles) ----------------
+        // ---------------- TMA producer (this CTA's x halves) ----------------
         if (lane == 0) {
             int last = -1;
             for (int it = 0; it < total_kb; ++it) {
                 const int s = it % kStages;
                 const uint32_t ph = (uint32_t)(it / kStages) & 1u;
                 if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-                const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+                const int t = pair + (it / p.kblocks) * npairs;
                 const int kb = it % p.kblocks;
-                const int tok0 = (t / p.w_tiles) * kTileT;
-                mbar_expect_tx(&full_x[s], kXBytes);
-                tma_load_2d(smem_x + s * kXBytes, &xmap, &full_x[s], kb * kBK, tok0);
-                tma_load_2d(smem_x + s * kXBytes + kXHalfBytes, &xmap, &full_x[s], kb * kBK, tok0 + kHalfT);
+                const int tok0 = tok_0(t) + (int)rank * kCtaT;
+                if (rank == 0) mbar_expect_tx(&full_x[s], 2 * kXBytes);   // both CTAs' bytes
+                const uint32_t lead = mapa(&full_x[s], 0);
+                tma_load_2d_pair(smem_x + s * kXBytes, &xmap, lead, kb * kBK, tok0);
+                tma_load_2d_pair(smem_x + s * kXBytes + kXHalfBytes, &xmap, lead, kb * kBK, tok0 + kHalfT);
                 last = it;
             }
             if (!*abort_flag) {
@@ -357,15 +421,25 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                     if (!mbar_wait(&empty[it % kStages], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) break;
                 }
             }
-            if (*abort_flag) {
+            if (*abort_flag && last >= 0) {
                 // Let every TMA still in flight land before the CTA exits.
-                for (int it = max(0, last - kStages + 1); it <= last; ++it)
-                    mbar_drain(&full_x[it % kStages], (uint32_t)(it / kStages) & 1u);
+                // The leader waits for its full_x phases (bounded: a phase the
+                // other CTA never filled gives up).  The other CTA's copies
+                // signal the leader's barrier, so it waits a fixed 100 us - an
+                // 8 KB copy lands in microseconds.
+                if (rank == 0) {
+                    for (int it = max(0, last - kStages + 1); it <= last; ++it)
+                        mbar_drain(&full_x[it % kStages], (uint32_t)(it / kStages) & 1u);
+                } else {
+                    const uint64_t t0 = globaltimer();
+                    while (globaltimer() - t0 < 100000ull) {
+                    }
+                }
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (leader) ----------------
+        if (lane == 0 && rank == 0) {
             int it = 0;
             bool issued_any = false;
             for (int lt = 0; lt < my_tiles && !*abort_flag; ++lt) {
@@ -386,18 +460,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                     for (int k16 = 0; k16 < kBK / 16; ++k16) {
                         const uint32_t acc = (kb > 0 || k16 > 0) ? 1u : 0u;
                         const uint64_t ad = sw64_desc(wa + k16 * 32);
-                        mma_bf16(tmem_base, ad, sw64_desc(xa + k16 * 32), kIdesc, acc);
-                        mma_bf16(tmem_base + kHalfT, ad, sw64_desc(xa + kXHalfBytes + k16 * 32), kIdesc, acc);
+                        mma_bf16_pair(tmem_base, ad, sw64_desc(xa + k16 * 32), kIdesc, acc);
+                        mma_bf16_pair(tmem_base + kHalfT, ad, sw64_desc(xa + kXHalfBytes + k16 * 32), kIdesc, acc);
                     }
                     issued_any = true;
-                    mma_commit(&empty[s]);
+                    mma_commit_pair(mapa(&empty[s], 0));
+                    mma_commit_pair(mapa(&empty[s], 1));
                 }
                 if (!ok) break;
-                mma_commit(tmem_full);
+                mma_commit_pair(mapa(tmem_full, 0));
+                mma_commit_pair(mapa(tmem_full, 1));
             }
             if (*abort_flag && issued_any) {
                 // Wait (bounded) for every MMA issued so far before TMEM is freed.
-                mma_commit(drain);
+                mma_commit_pair(mapa(drain, 0));
                 mbar_drain(drain, 0);
             }
         }
@@ -409,11 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                 const int s = it % kCStages;
                 const uint32_t ph = (uint32_t)(it / kCStages) & 1u;
                 if (!mbar_wait(&cempty[s], ph ^ 1u, abort_flag)) break;
-                const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+                const int t = pair + (it / p.kblocks) * npairs;
                 const int kb = it % p.kblocks;
                 mbar_expect_tx(&cfull[s], kCBytes);
-                tma_load_2d(smem_c + s * kCBytes, &cmap, &cfull[s], kb * CodeTile<FMT>::kRowBytes,
-                            (t % p.w_tiles) * kTileW);
+                tma_load_2d(smem_c + s * kCBytes, &cmap, &cfull[s], kb * CodeTile<FMT>::kRowBytes, w_row0(t));
                 last = it;
             }
             // Every fill must land before the CTA exits (the dequant warps
@@ -432,14 +507,15 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         const bool up_warp = q >= 2;
         float* x_out = smem_xch + ((q & 1) * 2 + (up_warp ? 0 : 1)) * 32 * 17;
         const float* x_in = smem_xch + ((q & 1) * 2 + (up_warp ? 1 : 0)) * 32 * 17;
+        const uint32_t lead_tmem_empty = mapa(tmem_empty, 0);
         uint32_t xc = 0;
         bool live = true;
         for (int lt = 0; lt < my_tiles && live; ++lt) {
             if (!mbar_wait(tmem_full, (uint32_t)lt & 1u, abort_flag)) break;
             tc_fence_after();
-            const int t = (int)blockIdx.x + lt * (int)gridDim.x;
-            const int w_row = (t % p.w_tiles) * kTileW + q * 32 + lane;
-            const int tok0 = (t / p.w_tiles) * kTileT;
+            const int t = pair + lt * npairs;
+            const int w_row = w_row0(t) + q * 32 + lane;
+            const int tok0 = tok_0(t);
 #pragma unroll 1
             for (int c = 0; c < kTileT / 32; ++c) {
                 if (tok0 + c * 32 >= p.m) break;        // uniform across the warp
@@ -454,7 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xch_full);
                     if (!mbar_wait(xch_full, xc & 1u, abort_flag)) { live = false; break; }
-                    const int64_t hc = (int64_t)(t % p.w_tiles) * 64 + (q & 1) * 32 + lane;
+                    // This CTA's 128 rows are one interleaved gate / up block.
+                    const int64_t hc = (int64_t)(w_row0(t) / kTileW) * 64 + (q & 1) * 32 + lane;
                     if (hc < p.swiglu_n) {
                         uint16_t* hp = p.y + (int64_t)(tok0 + c * 32) * p.ldy + hc;
 #pragma unroll
@@ -482,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tmem_empty);
+            if (lane == 0) mbar_arrive_cluster(lead_tmem_empty);
         }
     } else if (warp >= 8) {
         // ---------------- dequant: codes -> bf16 A tiles ----------------
@@ -492,10 +569,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         const int r = (warp - 8) * 8 + (lane >> 2); // row within the tile
         const int qd = lane & 3;                    // k quarter of the block: codes [8 qd, 8 qd + 8)
         auto coords = [&](int it, int* row, int* kk) {
-            const int t = (int)blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
-            *row = (t % p.w_tiles) * kTileW + r;
+            const int t = pair + (it / p.kblocks) * npairs;
+            *row = w_row0(t) + r;
             *kk = (it % p.kblocks) * kBK + 8 * qd;
         };
+        const uint32_t lead_full_w0 = mapa(&full_w[0], 0);
         // Scale bytes are prefetched four k-blocks ahead.
         uint32_t sc[4];
         int row, kk;
@@ -533,14 +611,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             *reinterpret_cast<uint4*>(smem_w + s * kWBytes + w_off) = o;
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full_w[s]);
+            if (lane == 0) mbar_arrive_cluster(lead_full_w0 + (uint32_t)(s * sizeof(uint64_t)));
         }
     }
 
+    // The pair meets before TMEM is freed: the leader's MMAs write the other
+    // CTA's TMEM and read its shared memory, and the other CTA's arrives and
+    // copies target the leader's barriers.
     __syncthreads();
+    cluster_sync();
     if (warp == 2) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
     }
 }
 
@@ -560,7 +642,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int FMT>
-int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int grid, cudaStream_t stream) {
+int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int pairs, cudaStream_t stream) {
     // Code tiles: u8 [N rows, K*bits/8 bytes] with row stride ldc, box
     // [128 rows x 32 k], swizzled to match read_codes().
     CUtensorMap cmap;
@@ -580,8 +662,30 @@ int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, in
                                           kSmemBytes));
         configured[dev] = true;
     }
-    qmm_gemm_kernel<FMT><<<grid, kThreads, kSmemBytes, stream>>>(map, cmap, p);
-    QMM_CUDA_TRY(cudaGetLastError());
+    // Pairs of CTAs (clusters of 2), at most as many pairs as fit on the
+    // device at once (a GPC with an odd number of free SMs leaves one idle).
+    static int max_pairs[64] = {0};
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (dev < 64 && max_pairs[dev] == 0) {
+        cfg.gridDim = dim3((unsigned)(2 * pairs));
+        int n = 0;
+        QMM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, qmm_gemm_kernel<FMT>, &cfg));
+        if (n < 1) return set_error(QMM_ERR_CUDA, "no CTA pair of the prefill GEMM fits on the device");
+        max_pairs[dev] = n;
+    }
+    const int npairs = dev < 64 ? std::min(pairs, max_pairs[dev]) : 1;
+    cfg.gridDim = dim3((unsigned)(2 * npairs));
+    QMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qmm_gemm_kernel<FMT>, map, cmap, p));
     return QMM_OK;
 }
 
@@ -606,7 +710,7 @@ int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     CUtensorMap map;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
     const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kHalfT};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kCtaT};
     const cuuint32_t estride[2] = {1, 1};
     CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box,
                          estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
@@ -618,15 +722,15 @@ int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     p.ldc = a.ldc; p.lds = a.lds; p.ldy = a.ldy;
     p.m = (int)a.m; p.n = (int)a.n; p.k = (int)a.k;
     p.kblocks = (p.k + kBK - 1) / kBK;
-    p.w_tiles = (p.n + kTileW - 1) / kTileW;
+    p.w_tiles = (p.n + kPairW - 1) / kPairW;
     p.swiglu_n = (int)a.swiglu_n;
     if (a.swiglu_n > 0 && (a.n % kTileW)) return QMM_OK;   // gate / up tiles are whole 64 + 64 blocks
     const int64_t tiles = (int64_t)p.w_tiles * ((p.m + kTileT - 1) / kTileT);
     if (tiles > INT32_MAX) return QMM_OK;
     p.num_tiles = (int)tiles;
-    const int grid = (int)std::min<int64_t>(tiles, info.sms);
-    int rc = a.fmt == kMXFP8 ? launch_fmt<kMXFP8>(a, p, map, grid, stream)
-                             : launch_fmt<kNVFP4>(a, p, map, grid, stream);
+    const int pairs = (int)std::min<int64_t>(tiles, info.sms / 2);
+    int rc = a.fmt == kMXFP8 ? launch_fmt<kMXFP8>(a, p, map, pairs, stream)
+                             : launch_fmt<kNVFP4>(a, p, map, pairs, stream);
     if (rc == QMM_OK) *handled = true;
     return rc;
 }
