@@ -13,26 +13,27 @@
 //
 // The expensive step is the dequantisation (the fp8/fp4 -> f16 conversions
 // run at a quarter of the fp32 rate on sm_100), so the tile is shaped to
-// dequantise each code once per 512 tokens, and x - re-read from L2 by every
+// dequantise each code once per 512 tokens, the k-blocks are 64 wide (16
+// codes per dequant thread per hand-over), and x - re-read from L2 by every
 // weight tile - is split across a CTA pair.  Two CTAs of a cluster (one per
 // SM, persistent) compute y^T tiles of 256 weight rows x 512 tokens with
-// tcgen05.mma.cta_group::2: per 32-wide k-block, each CTA dequantises its
+// tcgen05.mma.cta_group::2: per 64-wide k-block, each CTA dequantises its
 // own 128 weight rows (its half of the M = 256 A operand) and loads its
 // 128-token half of each of the two 256-token B operands, so a CTA moves
-// 16 KB of x per k-block instead of 32 KB.  The pair's leader (cluster rank
+// 32 KB of x per k-block instead of 64 KB.  The pair's leader (cluster rank
 // 0) issues two MMAs of 256 x 256 x 16 per k16 step; each CTA's TMEM holds
 // its 128 rows x 512 tokens in fp32 (all 512 columns).  Warp roles (24
 // warps, both CTAs):
-//   warp 0      TMA producer: this CTA's x halves [2 x 128 tokens x 32 k],
-//               64B swizzle, counted on the leader's full_x barrier
+//   warp 0      TMA producer: this CTA's x halves [2 x 128 tokens x 64 k],
+//               128B swizzle, counted on the leader's full_x barrier
 //   warp 1      MMA issuer (leader only): tcgen05.mma.cta_group::2 kind::f16
 //   warp 2      TMEM allocator (512 columns in each CTA, cta_group::2)
-//   warp 3      TMA producer: W code tiles [128 rows x 32 k] (own ring)
+//   warp 3      TMA producer: W code tiles [128 rows x 64 k] (own ring)
 //   warps 4-7   epilogue: tcgen05.ld -> bf16 -> y (coalesced 64-byte rows)
-//   warps 8-23  dequant: 8 codes per thread per k-block from the code ring,
+//   warps 8-23  dequant: 16 codes per thread per k-block from the code ring,
 //               scale bytes prefetched from global memory, decoded with
 //               cvt.{e4m3x2,e2m1x2}, written as bf16 into the A tile in the
-//               UMMA K-major 64B-swizzle layout
+//               UMMA K-major 128B-swizzle layout
 // Pipelines (mbarriers): kStages stages of {x halves, W tile}.  On the
 // leader: full_x (both CTAs' TMA bytes), full_w (both CTAs' 16 dequant
 // warps), tmem_empty (both CTAs' 4 epilogue warps).  In each CTA: empty and
@@ -61,18 +62,18 @@ __device__ unsigned int g_device_error = 0;
 
 namespace {
 
-constexpr int kStages = 7;
-constexpr int kBK = 32;                     // k per stage (64 bytes of bf16: one 64B swizzle row)
+constexpr int kStages = 4;
+constexpr int kBK = 64;                     // k per stage (128 bytes of bf16: one 128B swizzle row)
 constexpr int kTileW = 128;                 // weight rows per CTA (half the pair's MMA M)
 constexpr int kPairW = 2 * kTileW;          // weight rows per pair tile (MMA M)
 constexpr int kHalfT = 256;                 // tokens per MMA (MMA N)
 constexpr int kTileT = 2 * kHalfT;          // tokens per tile
 constexpr int kCtaT = kHalfT / 2;           // tokens of one MMA's B operand held by each CTA
 constexpr int kThreads = 768;
-constexpr int kXHalfBytes = kCtaT * kBK * 2;    // 8 KB
-constexpr int kXBytes = 2 * kXHalfBytes;        // 16 KB per CTA per stage
-constexpr int kWBytes = kTileW * kBK * 2;       // 8 KB
-constexpr int kCodeRingBytes = 32768;
+constexpr int kXHalfBytes = kCtaT * kBK * 2;    // 16 KB
+constexpr int kXBytes = 2 * kXHalfBytes;        // 32 KB per CTA per stage
+constexpr int kWBytes = kTileW * kBK * 2;       // 16 KB
+constexpr int kCodeRingBytes = 16384;
 // SwiGLU epilogue: a gate-row warp and its up-row warp swap half of each
 // 32 x 32 fp32 accumulator chunk (rows padded to 17 words), both ways.
 constexpr int kXchBytes = 2 * 2 * 32 * 17 * 4;
@@ -230,16 +231,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// UMMA shared-memory descriptor: K-major, 64-byte swizzle (8-row atoms of
-// 512 bytes, SBO), version 1 (sm_100).  The 16-byte chunk c of row r of a
-// tile sits at r * 64 + ((c ^ ((r >> 1) & 3)) * 16) (tile base 1024-aligned).
-__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle (8-row atoms of
+// 1024 bytes, SBO), version 1 (sm_100).  The 16-byte chunk c of row r of a
+// tile sits at r * 128 + ((c ^ (r & 7)) * 16) (tile base 1024-aligned); a
+// k16 step advances the start address by 32 bytes within the row.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)1 << 16;                    // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(512 >> 4) << 32;           // SBO: 8 rows x 64 bytes
+    d |= (uint64_t)(1024 >> 4) << 32;          // SBO: 8 rows x 128 bytes
     d |= (uint64_t)1 << 46;                    // descriptor version
-    d |= (uint64_t)4 << 61;                    // SWIZZLE_64B
+    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
     return d;
 }
 
@@ -249,19 +251,20 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kHa
                             ((uint32_t)(kPairW >> 4) << 24);
 
 // ---- W code tiles --------------------------------------------------------------
-// [128 rows x 32 k] per k-block, by TMA into their own ring: 32 bytes per row
-// (mxfp8, 32B swizzle: chunk ^= (r >> 2) & 1) or 16 bytes (nvfp4, unswizzled).
+// [128 rows x 64 k] per k-block, by TMA into their own ring: 64 bytes per row
+// (mxfp8, 64B swizzle) or 32 bytes (nvfp4, 32B swizzle).
 template <int FMT> struct CodeTile;
 template <> struct CodeTile<kMXFP8> {
+    static constexpr int kRowBytes = 64;
+    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_64B;
+};
+template <> struct CodeTile<kNVFP4> {
     static constexpr int kRowBytes = 32;
     static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_32B;
 };
-template <> struct CodeTile<kNVFP4> {
-    static constexpr int kRowBytes = 16;
-    static constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
-};
 
-// Scale byte of a thread's 8 codes (k [kk, kk + 8) of one row), prefetched
+// Scale byte of a thread's 16 codes (k [kk, kk + 16) of one row: one nvfp4
+// group, half an mxfp8 group), prefetched
 // ahead from global memory in the checkpoint layout; 0 outside the matrix.
 template <int FMT>
 __device__ __forceinline__ uint32_t load_scale(const GemmParams& p, int row, int kk) {
@@ -269,14 +272,16 @@ __device__ __forceinline__ uint32_t load_scale(const GemmParams& p, int row, int
     return __ldg(p.scales + (int64_t)row * p.lds + kk / (FMT == kMXFP8 ? 32 : 16));
 }
 
-// Row r's 8 codes for k eighth q (codes [8q, 8q + 8) of the k-block).
+// Row r's 16 codes for k quarter q (codes [16q, 16q + 16) of the k-block):
+// mxfp8 one 16-byte chunk of a 64-byte row (64B swizzle: chunk ^= (r >> 1) & 3),
+// nvfp4 8 bytes of a 32-byte row (32B swizzle: chunk ^= (r >> 2) & 1).
 template <int FMT>
-__device__ __forceinline__ uint2 read_codes(const uint8_t* tile, int r, int q) {
+__device__ __forceinline__ uint4 read_codes(const uint8_t* tile, int r, int q) {
     if constexpr (FMT == kMXFP8) {
-        const int sw = (r >> 2) & 1;
-        return *reinterpret_cast<const uint2*>(tile + r * 32 + (((q >> 1) ^ sw) << 4) + (q & 1) * 8);
+        return *reinterpret_cast<const uint4*>(tile + r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
     } else {
-        return make_uint2(*reinterpret_cast<const uint32_t*>(tile + r * 16 + 4 * q), 0u);
+        const uint2 v = *reinterpret_cast<const uint2*>(tile + r * 32 + (((q >> 1) ^ ((r >> 2) & 1)) << 4) + (q & 1) * 8);
+        return make_uint4(v.x, v.y, 0u, 0u);
     }
 }
 
@@ -459,9 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
 #pragma unroll
                     for (int k16 = 0; k16 < kBK / 16; ++k16) {
                         const uint32_t acc = (kb > 0 || k16 > 0) ? 1u : 0u;
-                        const uint64_t ad = sw64_desc(wa + k16 * 32);
-                        mma_bf16_pair(tmem_base, ad, sw64_desc(xa + k16 * 32), kIdesc, acc);
-                        mma_bf16_pair(tmem_base + kHalfT, ad, sw64_desc(xa + kXHalfBytes + k16 * 32), kIdesc, acc);
+                        const uint64_t ad = sw128_desc(wa + k16 * 32);
+                        mma_bf16_pair(tmem_base, ad, sw128_desc(xa + k16 * 32), kIdesc, acc);
+                        mma_bf16_pair(tmem_base + kHalfT, ad, sw128_desc(xa + kXHalfBytes + k16 * 32), kIdesc, acc);
                     }
                     issued_any = true;
                     mma_commit_pair(mapa(&empty[s], 0));
@@ -567,11 +572,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
         // its scale byte (one sector per row), and the warp's code reads and
         // W-tile writes are contiguous 128 / 256 / 512-byte runs.
         const int r = (warp - 8) * 8 + (lane >> 2); // row within the tile
-        const int qd = lane & 3;                    // k quarter of the block: codes [8 qd, 8 qd + 8)
+        const int qd = lane & 3;                    // k quarter of the block: codes [16 qd, 16 qd + 16)
         auto coords = [&](int it, int* row, int* kk) {
             const int t = pair + (it / p.kblocks) * npairs;
             *row = w_row0(t) + r;
-            *kk = (it % p.kblocks) * kBK + 8 * qd;
+            *kk = (it % p.kblocks) * kBK + 16 * qd;
         };
         const uint32_t lead_full_w0 = mapa(&full_w[0], 0);
         // Scale bytes are prefetched four k-blocks ahead.
@@ -585,8 +590,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
                 sc[i] = load_scale<FMT>(p, row, kk);
             }
         }
-        // This thread's 16-byte bf16 chunk of a W tile row (64B swizzle).
-        const uint32_t w_off = (uint32_t)(r * 64 + ((qd ^ ((r >> 1) & 3)) << 4));
+        // This thread's two 16-byte bf16 chunks of a W tile row (128B swizzle).
+        const uint32_t w_off0 = (uint32_t)(r * 128 + (((2 * qd) ^ (r & 7)) << 4));
+        const uint32_t w_off1 = (uint32_t)(r * 128 + (((2 * qd + 1) ^ (r & 7)) << 4));
         for (int it = 0; it < total_kb; ++it) {
             const uint32_t cur = sc[0];
             sc[0] = sc[1];
@@ -601,14 +607,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemm_kernel(const __grid_cons
             const uint32_t ph = (uint32_t)(it / kStages) & 1u;
             const int cs = it % kCStages;
             if (!mbar_wait(&cfull[cs], (uint32_t)(it / kCStages) & 1u, abort_flag)) break;
-            const uint2 codes = read_codes<FMT>(smem_c + cs * kCBytes, r, qd);
+            const uint4 codes = read_codes<FMT>(smem_c + cs * kCBytes, r, qd);
             __syncwarp();
             if (lane == 0) mbar_arrive(&cempty[cs]);
             // Codes outside the matrix are zero (TMA fill) and their scale
             // byte reads as 0, so the chunk is exactly zero.
-            const uint4 o = dequant8<FMT>(codes, cur);
+            const uint4 o0 = FMT == kMXFP8 ? dequant8<FMT>(make_uint2(codes.x, codes.y), cur)
+                                           : dequant8<FMT>(make_uint2(codes.x, 0u), cur);
+            const uint4 o1 = FMT == kMXFP8 ? dequant8<FMT>(make_uint2(codes.z, codes.w), cur)
+                                           : dequant8<FMT>(make_uint2(codes.y, 0u), cur);
             if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) break;
-            *reinterpret_cast<uint4*>(smem_w + s * kWBytes + w_off) = o;
+            *reinterpret_cast<uint4*>(smem_w + s * kWBytes + w_off0) = o0;
+            *reinterpret_cast<uint4*>(smem_w + s * kWBytes + w_off1) = o1;
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_full_w0 + (uint32_t)(s * sizeof(uint64_t)));
@@ -644,7 +654,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int FMT>
 int launch_fmt(const QmmArgs& a, const GemmParams& p, const CUtensorMap& map, int pairs, cudaStream_t stream) {
     // Code tiles: u8 [N rows, K*bits/8 bytes] with row stride ldc, box
-    // [128 rows x 32 k], swizzled to match read_codes().
+    // [128 rows x 64 k], swizzled to match read_codes().
     CUtensorMap cmap;
     const cuuint64_t cdim[2] = {(cuuint64_t)(a.k * (FMT == kMXFP8 ? 8 : 4) / 8), (cuuint64_t)a.n};
     const cuuint64_t cstride[1] = {(cuuint64_t)a.ldc};
@@ -706,14 +716,14 @@ int launch_gemm(const QmmArgs& a, cudaStream_t stream, bool* handled) {
     if (int rc = device_info(dev, &info)) return rc;
     if (info.smem_optin < (size_t)kSmemBytes) return QMM_OK;
 
-    // x tiles: bf16 [M rows, K] with row stride ldx, box [256 rows x 32 k], 64B swizzle.
+    // x tiles: bf16 [M rows, K] with row stride ldx, box [128 rows x 64 k], 128B swizzle.
     CUtensorMap map;
     const cuuint64_t gdim[2] = {(cuuint64_t)a.k, (cuuint64_t)a.m};
     const cuuint64_t gstride[1] = {(cuuint64_t)(a.ldx * 2)};
     const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kCtaT};
     const cuuint32_t estride[2] = {1, 1};
     CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(a.x), gdim, gstride, box,
-                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_error(QMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
 
