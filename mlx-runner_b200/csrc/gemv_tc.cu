@@ -223,8 +223,9 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
 //               the k rows hold) x x row t.  The block-diagonal x makes each
 //               accumulator column one group's partial sum, scaled after the
 //               mma in fp32.  M <= 2.
-//               (A two-mma form for M <= 4, n = 4 q + t, measured slower
-//               than kXlTokens at M = 3, 4.)
+//               (Measured slower than kXlTokens at M = 3, 4: a two-mma form,
+//               n = 4 q + t, and a one-mma form with two group slots of four
+//               x rows, the slot's two lanes swapping half their code words.)
 constexpr int kXlTokens = 0, kXlGroups2 = 1;
 
 // Epilogue of a finished row block: y (bf16, or fp32 partial sums), the
@@ -289,21 +290,27 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
     // whose range holds a row-block boundary therefore takes fewer units.
     // Unit u belongs to CTA owner(u).  32-bit division when the products fit
     // (64-bit division is a long software sequence).
-    const unsigned G = gridDim.x;
-    const int kcg = p.kchunks + p.gap;
-    const int64_t V = (int64_t)p.row_blocks * kcg;
-    const bool fits32 = (uint64_t)(V + 1) * G < (1ull << 32);
+    // The helpers recompute the slot count from p and gridDim (a few integer
+    // operations per call, at flush time) so that it holds no register
+    // through the unit loop (held, it cost the M <= 2 kernel spills and
+    // 0.4 us per launch).
+    auto slot_count = [&]() -> int64_t { return (int64_t)p.row_blocks * (p.kchunks + p.gap); };
+    auto fits32 = [&]() -> bool { return (uint64_t)(slot_count() + 1) * gridDim.x < (1ull << 32); };
     auto unit_of_slot = [&](int64_t v) -> int {          // first unit at or after slot v
         if (p.gap == 0) return (int)v;
-        const unsigned rb = (unsigned)v / (unsigned)kcg, o = (unsigned)v - rb * (unsigned)kcg;
+        const unsigned kcg = (unsigned)(p.kchunks + p.gap);
+        const unsigned rb = (unsigned)v / kcg, o = (unsigned)v - rb * kcg;
         return (int)(rb * (unsigned)p.kchunks + min(o, (unsigned)p.kchunks));
     };
     auto first_unit = [&](int j) -> int {
-        return unit_of_slot(fits32 ? (int64_t)(((unsigned)V * (unsigned)j) / G) : (V * j) / G);
+        const int64_t V = slot_count();
+        return unit_of_slot(fits32() ? (int64_t)(((unsigned)V * (unsigned)j) / gridDim.x) : (V * j) / gridDim.x);
     };
     auto owner = [&](int u) -> int {
-        const int64_t v = p.gap == 0 ? u : (int64_t)(u / p.kchunks) * kcg + u % p.kchunks;
-        return fits32 ? (int)(((unsigned)(v + 1) * G - 1u) / (unsigned)V) : (int)(((v + 1) * G - 1) / V);
+        const int64_t V = slot_count();
+        const int64_t v = p.gap == 0 ? u : (int64_t)(u / p.kchunks) * (p.kchunks + p.gap) + u % p.kchunks;
+        return fits32() ? (int)(((unsigned)(v + 1) * gridDim.x - 1u) / (unsigned)V)
+                        : (int)(((v + 1) * gridDim.x - 1) / V);
     };
     const int u0 = first_unit((int)blockIdx.x);
     const int u1 = first_unit((int)blockIdx.x + 1);
