@@ -676,11 +676,23 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             if (!*s_last) return;
             const int col = t >> 6, j = t & 63;
             float M = -INFINITY, S = 0.0f;
-            if (col < p.m)
-                for (int i = j; i < 2 * p.row_blocks; i += 64) {
-                    const float2 ps = __ldcg(&p.am_part[((int64_t)(i >> 1) * 8 + col) * 2 + (i & 1)]);
-                    lse_merge(M, S, ps.x, ps.y);
+            if (col < p.m) {
+                // Eight loads in flight per batch (the pairs are an L2 round
+                // trip each; one at a time they cost tens of microseconds on
+                // the 248320-row head), merged in index order.
+                const int total = 2 * p.row_blocks;
+                for (int i0 = j; i0 < total; i0 += 64 * 8) {
+                    float2 ps[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int i = i0 + 64 * q;
+                        ps[q] = i < total ? __ldcg(&p.am_part[((int64_t)(i >> 1) * 8 + col) * 2 + (i & 1)])
+                                          : make_float2(-INFINITY, 0.0f);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) lse_merge(M, S, ps[q].x, ps[q].y);
                 }
+            }
 #pragma unroll
             for (int o = 16; o; o >>= 1) {
                 const float m2 = __shfl_xor_sync(0xFFFFFFFFu, M, o), s2 = __shfl_xor_sync(0xFFFFFFFFu, S, o);
