@@ -590,14 +590,29 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_tc_kernel(const __grid_c
             for (int q = 0; q < n_list; ++q) {
                 const int rb = s_tp_list[1 + 2 * q];
                 const int64_t par = (unsigned int)s_tp_list[2 + 2 * q] & 1u;
+                // Every rank's value of both outputs is loaded before any is
+                // added (2 P loads in flight instead of a chain of 2 P round
+                // trips), then summed in rank order.
+                float v[2][kMaxTpRanks];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int idx = t + 512 * e, col = idx & 7, row = rb * kRows + (idx >> 3);
+                    const bool ok = row < p.n && col < p.m;
+#pragma unroll
+                    for (int src = 0; src < kMaxTpRanks; ++src)
+                        v[e][src] = ok && src < P
+                                        ? __ldcg(p.tp_recv[me] + (par * P + src) * p.tp_cap + (int64_t)col * p.n + row)
+                                        : 0.f;
+                }
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int idx = t + 512 * e, col = idx & 7, row = rb * kRows + (idx >> 3);
                     if (row < p.n && col < p.m) {
-                        float v = 0.f;
-                        for (int src = 0; src < P; ++src)
-                            v += __ldcg(p.tp_recv[me] + (par * P + src) * p.tp_cap + (int64_t)col * p.n + row);
-                        p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(v);
+                        float sum = 0.f;
+#pragma unroll
+                        for (int src = 0; src < kMaxTpRanks; ++src)
+                            if (src < P) sum += v[e][src];
+                        p.y[(int64_t)col * p.ldy + row] = f32_to_bf16(sum);
                     }
                 }
             }
