@@ -839,6 +839,7 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA-graph replays")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM (profiling runs)")
+    ap.add_argument("--lm-head-only", action="store_true", help="only the lm_head decode GEMV (profiling runs)")
     ap.add_argument("--prefill-m", type=int, default=PREFILL["m"])
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-warmup", type=int, default=2)
@@ -881,6 +882,30 @@ def main() -> None:
         t = torch.tensor([v], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.lm_head_only:
+        # Profiling runs: the decode kernel streaming the 716 MB lm_head
+        # ([248320, 5120] nvfp4, M = 1), the longest single decode launch, so
+        # that a capture of one launch shows the kernel's steady streaming rate.
+        codes, scales = _quantized_normal(qmm, 248320, 5120, "nvfp4", dev, seed=3)
+        w = qmm.QuantizedWeight(codes, scales, "nvfp4")
+        del codes, scales
+        x = torch.randn((1, 5120), device=dev).to(torch.bfloat16)
+        y = torch.empty((1, 248320), device=dev, dtype=torch.bfloat16)
+        for _ in range(args.warmup):
+            w(x, out=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            w(x, out=y)
+        e1.record()
+        torch.cuda.synchronize()
+        qmm.device_status()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        nb = 248320 * 5120 // 2 + 248320 * 5120 // 16 + 2 * 5120 + 2 * 248320
+        print(json.dumps({"lm_head": {"us": us, "GBs": nb / (us * 1e-6) / 1e9, "steps": args.steps}}), flush=True)
+        w.close()
+        return
 
     if args.prefill_only:
         pf = prefill_measure(args, qmm, dev, world, rank, barrier, max_over_ranks)
