@@ -362,6 +362,37 @@ int gemm_bs_sf_bytes(int64_t n, int64_t k) {
     return (int)std::min<int64_t>(INT32_MAX, tiles * kblocks * kBsSfaBytes);
 }
 
+// The library's own stream-ordered pool per device for the per-call x
+// scratch.  The device's default pool gives its memory back at every
+// synchronisation (release threshold 0), so the next call could pay for
+// mapping it again - milliseconds per call; this pool keeps what it has
+// reserved (the largest call's scratch) until the process exits, and
+// leaves the default pool, which other code may use, as it is.
+static int scratch_pool(int dev, cudaMemPool_t* out) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    if (dev < 0 || dev >= 64) return set_error(QMM_ERR_BAD_ARGUMENT, "device %d is out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        QMM_CUDA_TRY(cudaMemPoolCreate(&pool, &props));
+        uint64_t keep = UINT64_MAX;
+        cudaError_t e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(pool);
+            return cuda_error(e, "cudaMemPoolSetAttribute(release threshold)");
+        }
+        pools[dev] = pool;
+    }
+    *out = pools[dev];
+    return QMM_OK;
+}
+
 int launch_gemm_blockscaled(const QmmArgs& a, const uint8_t* w_sf, cudaStream_t stream) {
     if (a.fmt != kNVFP4) return set_error(QMM_ERR_BAD_ARGUMENT, "the block-scaled GEMM takes nvfp4 weights");
     if (a.m < 1 || a.n < 1) return QMM_OK;
@@ -385,7 +416,9 @@ int launch_gemm_blockscaled(const QmmArgs& a, const uint8_t* w_sf, cudaStream_t 
     const int64_t xsf_bytes = t_tiles * kblocks * kBsSfbBytes;
     const int64_t off_s = (xc_bytes + 255) / 256 * 256, off_sf = off_s + (xs_bytes + 255) / 256 * 256;
     uint8_t* scratch = nullptr;
-    QMM_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), (size_t)(off_sf + xsf_bytes), stream));
+    cudaMemPool_t pool = nullptr;
+    if (int rc0 = scratch_pool(dev, &pool)) return rc0;
+    QMM_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), (size_t)(off_sf + xsf_bytes), pool, stream));
     uint8_t* xcodes = scratch;
     uint8_t* xscales = scratch + off_s;
     uint8_t* xsf = scratch + off_sf;
